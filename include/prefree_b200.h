@@ -1,0 +1,206 @@
+/*
+ * prefree_b200.h — C ABI of the B200 (sm_100a) CSR SpMV library.
+ *
+ * y = alpha * A * x + beta * y, A in CSR (0-based), fp64 or fp32 values,
+ * int32 column indices, int32 or int64 row pointers. No preprocessing pass:
+ * every call works straight from (row_ptr, col_idx, val) as given.
+ *
+ * Drop-in map onto wang-luhan/preFree-public:
+ *   - the C++ entry point `preFreeSpMV` itself (include/PreFree.h:3-5,
+ *     defined at src/spmv_kernel/preFreeSpMV.cu:563-662) is declared, with the
+ *     identical signature and mangled name, in include/PreFree.h of this repo;
+ *   - pf_prefree_spmv_* below are the same calls with C linkage (for ctypes /
+ *     FFI callers), one per value/index type;
+ *   - pf_spmv_* are the device-pointer core the reference never exposed: its
+ *     driver hard-wires allocation + copies + launch (preFreeSpMV.cu:571-648);
+ *     these take device pointers, a stream, alpha and beta;
+ *   - pf_mmio_read replaces mmio_allinone (utilities/mmio.cpp:1547-1713,
+ *     include/mmio.h:177-179), the harness's Matrix Market -> CSR input path.
+ *
+ * Every function returns a pf_status; none exits the process (the reference's
+ * CUDA_CHECK_ERROR calls exit(), include/common.h:49-58). pf_last_error()
+ * gives the text of the calling thread's last failure.
+ */
+#ifndef PREFREE_B200_H
+#define PREFREE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum pf_status {
+  PF_OK = 0,
+  PF_ERR_INVALID = 1,     /* bad argument: size, null pointer, layout       */
+  PF_ERR_CUDA = 2,        /* a CUDA runtime call failed                     */
+  PF_ERR_DEVICE = 3,      /* a kernel reported an error word (see below)    */
+  PF_ERR_UNSUPPORTED = 4, /* valid request this build does not provide      */
+  PF_ERR_IO = 5,          /* file could not be opened / read                */
+  PF_ERR_FORMAT = 6       /* Matrix Market text could not be parsed         */
+} pf_status;
+
+/* Kernel variants (compile-time table, selected per call; AUTO = selector). */
+typedef enum pf_variant {
+  PF_VARIANT_AUTO = 0,
+  PF_VARIANT_NNZSPLIT = 1, /* nnz-balanced CTA slices, any row length        */
+  PF_VARIANT_ROWGROUP = 2  /* row-aligned slices, warp lanes per row (short) */
+} pf_variant;
+
+typedef struct pf_handle_s *pf_handle;
+
+const char *pf_last_error(void);
+const char *pf_version(void);
+/* Number of this library's kernels launched since it was loaded. */
+uint64_t pf_launch_count(void);
+
+/* A handle owns per-device scratch (cross-CTA carries for rows split between
+ * CTAs) and the device error word. It is bound to the device current at
+ * creation. Calls that share a handle must not overlap on the GPU (use one
+ * handle per stream). */
+pf_status pf_handle_create(pf_handle *out);
+pf_status pf_handle_destroy(pf_handle h);
+pf_status pf_handle_set_variant(pf_handle h, int variant);
+/* Testing knob: fixed non-zeros per CTA slice for NNZSPLIT (0 = automatic).
+ * Small slices force many rows to be cut between CTAs. */
+pf_status pf_handle_set_slice(pf_handle h, int64_t slice_nnz);
+/* Synchronizes the device, returns the device error bits, optionally clears. */
+pf_status pf_handle_device_error(pf_handle h, uint32_t *bits, int clear);
+
+/* ---- device-pointer core: y = alpha*A*x + beta*y ----------------------------
+ * row_ptr has m+1 entries; row_ptr[0] may be non-zero (a row slice of a larger
+ * CSR): val/col_idx are addressed with the absolute row_ptr values, and nnz
+ * must equal row_ptr[m] - row_ptr[0]. x has n entries, y has m. With beta == 0
+ * y is not read. `stream` is a cudaStream_t (NULL = legacy default stream).
+ * Asynchronous: returns after the launch. Accumulation is in fp64 for both
+ * value types; the result is rounded once to the value type. Deterministic:
+ * the same inputs give bit-identical y on every call.                         */
+pf_status pf_spmv_f64_i32(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                          const int32_t *row_ptr, const int32_t *col_idx,
+                          const double *val, double alpha, const double *x,
+                          double beta, double *y, void *stream);
+pf_status pf_spmv_f64_i64(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                          const int64_t *row_ptr, const int32_t *col_idx,
+                          const double *val, double alpha, const double *x,
+                          double beta, double *y, void *stream);
+pf_status pf_spmv_f32_i32(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                          const int32_t *row_ptr, const int32_t *col_idx,
+                          const float *val, double alpha, const float *x,
+                          double beta, float *y, void *stream);
+pf_status pf_spmv_f32_i64(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                          const int64_t *row_ptr, const int32_t *col_idx,
+                          const float *val, double alpha, const float *x,
+                          double beta, float *y, void *stream);
+
+/* ---- host-buffer call (one multiply, copies in and out) ---------------------
+ * Same arithmetic as pf_spmv_*, on HOST arrays: copies row_ptr/col/val/x in
+ * (and y when beta != 0), multiplies once, copies y out, synchronizes. Device
+ * buffers are cached in the handle and reused across calls. Pinned host memory
+ * gives full PCIe bandwidth; pageable memory works too.                       */
+pf_status pf_spmv_host_f64_i32(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                               const int32_t *row_ptr, const int32_t *col_idx,
+                               const double *val, double alpha,
+                               const double *x, double beta, double *y,
+                               void *stream);
+pf_status pf_spmv_host_f64_i64(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                               const int64_t *row_ptr, const int32_t *col_idx,
+                               const double *val, double alpha,
+                               const double *x, double beta, double *y,
+                               void *stream);
+pf_status pf_spmv_host_f32_i32(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                               const int32_t *row_ptr, const int32_t *col_idx,
+                               const float *val, double alpha, const float *x,
+                               double beta, float *y, void *stream);
+pf_status pf_spmv_host_f32_i64(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                               const int64_t *row_ptr, const int32_t *col_idx,
+                               const float *val, double alpha, const float *x,
+                               double beta, float *y, void *stream);
+
+/* ---- preFreeSpMV with C linkage ---------------------------------------------
+ * Replaces preFreeSpMV (include/PreFree.h:3-5; preFreeSpMV.cu:563-662) for
+ * FFI callers. Host arrays in; Y_val is overwritten with A*x; *cdTime = ms per
+ * multiply averaged over the timed launches (4000 after 200 warm-up, as at
+ * preFreeSpMV.cu:604-650; PF_PREFREE_ITERS / PF_PREFREE_WARMUP override);
+ * *cdPre = ms of the pre-pass, which here is only the host-side variant
+ * selection (there is no preprocessing kernel). Reads row_ptr[0..rowA] (the
+ * reference also copies one entry past it, preFreeSpMV.cu:580; this does not).
+ * The fp32 and int64 forms are the same call for the other types.            */
+pf_status pf_prefree_spmv_f64_i32(double *csrVal, int32_t *csrRowPtr,
+                                  int32_t *csrColInd, double *X_val,
+                                  double *Y_val, int32_t rowA, int32_t colA,
+                                  int32_t nnzA, double *cdTime, double *cdPre);
+pf_status pf_prefree_spmv_f64_i64(double *csrVal, int64_t *csrRowPtr,
+                                  int32_t *csrColInd, double *X_val,
+                                  double *Y_val, int64_t rowA, int64_t colA,
+                                  int64_t nnzA, double *cdTime, double *cdPre);
+pf_status pf_prefree_spmv_f32_i32(float *csrVal, int32_t *csrRowPtr,
+                                  int32_t *csrColInd, float *X_val,
+                                  float *Y_val, int32_t rowA, int32_t colA,
+                                  int32_t nnzA, double *cdTime, double *cdPre);
+
+/* ---- Matrix Market -> CSR (the harness input path) --------------------------
+ * Replaces mmio_allinone (utilities/mmio.cpp:1547-1713): same banner handling
+ * (real / integer / pattern = 1.0 / complex = real part), 1-based -> 0-based,
+ * symmetric and Hermitian inputs expanded (off-diagonal entries mirrored),
+ * entries of a row kept in file order (no sort), row_ptr has m+1 entries.
+ * Differences: 64-bit row_ptr and nnz, a multi-threaded parser, and errors are
+ * returned instead of printed. Arrays are malloc'd; free them with pf_free.  */
+pf_status pf_mmio_read(const char *path, int64_t *m, int64_t *n, int64_t *nnz,
+                       int *is_symmetric, int64_t **row_ptr, int32_t **col_idx,
+                       double **val);
+void pf_free(void *p);
+
+/* ---- row sharding (multi-GPU) -----------------------------------------------
+ * Equal-nnz row split: bounds[k] = first row r with row_ptr[r] - row_ptr[0]
+ * >= k*nnz/parts (k = 0..parts; bounds[0] = 0, bounds[parts] = m). Host
+ * row_ptr. No counterpart in the reference (single GPU only).               */
+pf_status pf_shard_bounds_i32(const int32_t *row_ptr, int64_t m, int parts,
+                              int64_t *bounds);
+pf_status pf_shard_bounds_i64(const int64_t *row_ptr, int64_t m, int parts,
+                              int64_t *bounds);
+
+/* ---- synthetic inputs (benchmark configs; no counterpart in the reference,
+ * which reads SuiteSparse .mtx files) -----------------------------------------
+ * Counter-based: row r of config `cfg` is a pure function of (seed, r), the
+ * same bits on host and device. cfg: 1 uniform 16/row 100k^2, 2 5-point
+ * Laplacian 2048^2, 3 power-law 4M^2, 4 2000/row 50k^2, 5 banded+uniform
+ * 32/row 2^26 (sizes overridable via m for cfg 1,3,4,5: pass m <= 0 for the
+ * config's own size). value_mode: 0 = the config's distribution, 1 = i % 15
+ * (the reference harness's initVec, include/common.h:126-133).              */
+typedef struct pf_gen_spec {
+  int cfg;
+  int value_mode;
+  uint64_t seed;
+  int64_t m;     /* rows (0 = config default) */
+  int64_t n;     /* cols (0 = config default) */
+  int64_t k;     /* nnz per row for fixed-length configs (0 = default) */
+} pf_gen_spec;
+
+/* Resolve the defaults of a spec (m, n, k filled in). */
+pf_status pf_gen_resolve(pf_gen_spec *spec);
+/* Row lengths are needed first: len[r - r0] for rows [r0, r1). Host. */
+pf_status pf_gen_row_lengths_host(const pf_gen_spec *spec, int64_t r0,
+                                  int64_t r1, int64_t *len);
+/* Fill rows [r0, r1) on the HOST: row_ptr (r1-r0+1 entries, starting at 0),
+ * col, val (fp64; fp32 callers round). Single thread per call. */
+pf_status pf_gen_rows_host(const pf_gen_spec *spec, int64_t r0, int64_t r1,
+                           int64_t *row_ptr, int32_t *col, double *val);
+pf_status pf_gen_x_host(const pf_gen_spec *spec, int64_t c0, int64_t c1,
+                        double *x);
+/* Number of non-zeros in rows [r0, r1) (host; sizes the buffers below). */
+pf_status pf_gen_count(const pf_gen_spec *spec, int64_t r0, int64_t r1,
+                       int64_t *nnz_out);
+/* Device generation of rows [r0, r1) into device buffers: row_ptr rebased to
+ * start at 0 (r1-r0+1 entries, int32 or int64), col/val sized by
+ * pf_gen_count, fp64 or fp32 values. Synchronizes `stream` before returning. */
+pf_status pf_gen_rows_device(const pf_gen_spec *spec, int64_t r0, int64_t r1,
+                             int index_bytes, void *row_ptr, int32_t *col,
+                             int value_bytes, void *val, void *stream);
+pf_status pf_gen_x_device(const pf_gen_spec *spec, int64_t c0, int64_t c1,
+                          int value_bytes, void *x, void *stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* PREFREE_B200_H */

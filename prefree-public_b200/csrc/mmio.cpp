@@ -1,0 +1,340 @@
+// Matrix Market -> CSR reader: the harness input path of the reference
+// (mmio_allinone, utilities/mmio.cpp:1547-1713), rebuilt as a parallel parser.
+//
+// Same results as the reference for coordinate files:
+//   * banner "%%MatrixMarket matrix coordinate <type> <symmetry>", tokens
+//     case-insensitive (mm_read_banner, mmio.cpp:246-330);
+//   * comment lines (leading '%') skipped before the "M N NZ" size line
+//     (mm_read_mtx_crd_size, mmio.cpp:416-447);
+//   * values: real as parsed (strtod, the conversion scanf's %lg uses),
+//     integer converted to double, pattern = 1.0, complex = real part
+//     (mmio.cpp:1602-1636);
+//   * 1-based -> 0-based (:1629-1630);
+//   * symmetric and hermitian files mirror every off-diagonal entry into the
+//     column's row (:1641-1648); skew-symmetric files are NOT mirrored (the
+//     reference tests only mm_is_symmetric / mm_is_hermitian);
+//   * CSR by counting sort in file order: entry k lands in row i after every
+//     earlier entry of row i, and its mirror lands in row j right after that
+//     (:1650-1695). Column order inside a row is therefore file order.
+// Differences: int64 row_ptr/nnz, the entry lines are parsed by several
+// threads, dense "array" files and malformed input return an error instead of
+// reading garbage.
+#include <algorithm>
+#include <cctype>
+#include <cerrno>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/prefree_b200.h"
+
+namespace pf {
+void set_error(const char *fmt, ...);
+}
+
+namespace {
+
+struct Entries {
+  std::vector<int32_t> ri, ci;
+  std::vector<double> v;
+};
+
+inline const char *skip_ws(const char *p, const char *end) {
+  while (p < end && (*p == ' ' || *p == '\t' || *p == '\r')) ++p;
+  return p;
+}
+
+// Parse one entry line [p, eol). Returns false on malformed input.
+inline bool parse_entry(const char *p, const char *eol, int nv, bool is_int,
+                        int64_t *i, int64_t *j, double *val) {
+  char buf[128];
+  const char *q = p;
+  auto next_token = [&](const char **tb, size_t *tl) -> bool {
+    q = skip_ws(q, eol);
+    if (q >= eol) return false;
+    const char *s = q;
+    while (q < eol && !std::isspace((unsigned char)*q)) ++q;
+    *tb = s;
+    *tl = (size_t)(q - s);
+    return true;
+  };
+  const char *tb;
+  size_t tl;
+  for (int f = 0; f < 2; ++f) {
+    if (!next_token(&tb, &tl) || tl >= sizeof(buf)) return false;
+    std::memcpy(buf, tb, tl);
+    buf[tl] = 0;
+    char *e = nullptr;
+    const long long x = std::strtoll(buf, &e, 10);
+    if (e == buf) return false;
+    (f == 0 ? *i : *j) = x;
+  }
+  if (nv == 0) {
+    *val = 1.0;
+    return true;
+  }
+  if (!next_token(&tb, &tl) || tl >= sizeof(buf)) return false;
+  std::memcpy(buf, tb, tl);
+  buf[tl] = 0;
+  char *e = nullptr;
+  if (is_int) {
+    const long long x = std::strtoll(buf, &e, 10);
+    if (e == buf) return false;
+    *val = (double)(int)x;
+  } else {
+    *val = std::strtod(buf, &e);
+    if (e == buf) return false;
+  }
+  return true;  // a complex file's imaginary part is ignored
+}
+
+// Equal-nnz row split (see the header).
+template <typename IT>
+pf_status shard_bounds(const IT *rp, int64_t m, int parts, int64_t *b) {
+  if (!rp || !b || m < 0 || parts < 1) {
+    pf::set_error("pf_shard_bounds: bad arguments");
+    return PF_ERR_INVALID;
+  }
+  const int64_t base = (int64_t)rp[0];
+  const int64_t z = (int64_t)rp[m] - base;
+  b[0] = 0;
+  for (int k = 1; k < parts; ++k) {
+    const int64_t target = base + (int64_t)((__int128)z * k / parts);
+    int64_t lo = 0, hi = m;  // first r with rp[r] >= target
+    while (lo < hi) {
+      const int64_t mid = (lo + hi) / 2;
+      if ((int64_t)rp[mid] >= target) hi = mid;
+      else lo = mid + 1;
+    }
+    b[k] = std::max(lo, b[k - 1]);
+  }
+  b[parts] = m;
+  return PF_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+void pf_free(void *p) { std::free(p); }
+
+pf_status pf_mmio_read(const char *path, int64_t *m_out, int64_t *n_out,
+                       int64_t *nnz_out, int *sym_out, int64_t **row_ptr_out,
+                       int32_t **col_out, double **val_out) {
+  if (!path || !m_out || !n_out || !nnz_out || !sym_out || !row_ptr_out || !col_out ||
+      !val_out) {
+    pf::set_error("pf_mmio_read: null argument");
+    return PF_ERR_INVALID;
+  }
+  FILE *f = std::fopen(path, "rb");
+  if (!f) {
+    pf::set_error("pf_mmio_read: cannot open %s: %s", path, std::strerror(errno));
+    return PF_ERR_IO;
+  }
+  std::fseek(f, 0, SEEK_END);
+  const long fsz = std::ftell(f);
+  std::fseek(f, 0, SEEK_SET);
+  std::string text((size_t)std::max(0L, fsz), '\0');
+  const size_t got = fsz > 0 ? std::fread(&text[0], 1, (size_t)fsz, f) : 0;
+  std::fclose(f);
+  if ((long)got != fsz) {
+    pf::set_error("pf_mmio_read: short read on %s", path);
+    return PF_ERR_IO;
+  }
+  const char *p = text.data();
+  const char *end = p + text.size();
+  auto line_end = [&](const char *s) {
+    const char *e = (const char *)std::memchr(s, '\n', (size_t)(end - s));
+    return e ? e : end;
+  };
+
+  // banner
+  const char *eol = line_end(p);
+  std::string banner(p, eol);
+  char t[5][64];
+  if (std::sscanf(banner.c_str(), "%63s %63s %63s %63s %63s", t[0], t[1], t[2], t[3], t[4]) != 5) {
+    pf::set_error("pf_mmio_read: bad banner");
+    return PF_ERR_FORMAT;
+  }
+  for (int k = 1; k < 5; ++k)
+    for (char *c = t[k]; *c; ++c) *c = (char)std::tolower((unsigned char)*c);
+  if (std::strncmp(t[0], "%%MatrixMarket", 14) != 0 || std::strcmp(t[1], "matrix") != 0) {
+    pf::set_error("pf_mmio_read: not a Matrix Market matrix file");
+    return PF_ERR_FORMAT;
+  }
+  if (std::strcmp(t[2], "coordinate") != 0) {
+    pf::set_error("pf_mmio_read: only coordinate (sparse) files are supported");
+    return PF_ERR_FORMAT;
+  }
+  int nv;
+  bool is_int = false;
+  if (!std::strcmp(t[3], "real")) nv = 1;
+  else if (!std::strcmp(t[3], "integer")) { nv = 1; is_int = true; }
+  else if (!std::strcmp(t[3], "complex")) nv = 2;
+  else if (!std::strcmp(t[3], "pattern")) nv = 0;
+  else {
+    pf::set_error("pf_mmio_read: unknown data type %s", t[3]);
+    return PF_ERR_FORMAT;
+  }
+  const bool sym = !std::strcmp(t[4], "symmetric") || !std::strcmp(t[4], "hermitian");
+
+  // comments, then the size line
+  p = eol < end ? eol + 1 : end;
+  long long M = 0, N = 0, NZ = 0;
+  while (p < end) {
+    eol = line_end(p);
+    const char *q = skip_ws(p, eol);
+    if (q < eol && *q == '%') { p = eol + 1; continue; }
+    if (q >= eol) { p = eol + 1; continue; }  // blank line
+    std::string sl(q, eol);
+    if (std::sscanf(sl.c_str(), "%lld %lld %lld", &M, &N, &NZ) != 3) {
+      pf::set_error("pf_mmio_read: bad size line");
+      return PF_ERR_FORMAT;
+    }
+    p = eol < end ? eol + 1 : end;
+    break;
+  }
+  if (M <= 0 || N <= 0 || NZ < 0 || M > INT32_MAX || N > INT32_MAX) {
+    pf::set_error("pf_mmio_read: bad sizes M=%lld N=%lld NZ=%lld", M, N, NZ);
+    return PF_ERR_FORMAT;
+  }
+
+  // split the entry region into line-aligned chunks, count entries per chunk
+  unsigned nthr = std::max(1u, std::min(64u, std::thread::hardware_concurrency()));
+  if ((size_t)(end - p) < (1u << 20)) nthr = 1;
+  std::vector<const char *> cut(nthr + 1);
+  cut[0] = p;
+  for (unsigned k = 1; k < nthr; ++k) {
+    const char *c = p + (size_t)(end - p) * k / nthr;
+    if (c < cut[k - 1]) c = cut[k - 1];
+    const char *e = (const char *)std::memchr(c, '\n', (size_t)(end - c));
+    cut[k] = e ? e + 1 : end;
+  }
+  cut[nthr] = end;
+  auto is_entry_line = [](const char *s, const char *e) {
+    s = skip_ws(s, e);
+    return s < e && *s != '%';
+  };
+  std::vector<int64_t> cnt(nthr + 1, 0);
+  {
+    std::vector<std::thread> th;
+    for (unsigned k = 0; k < nthr; ++k)
+      th.emplace_back([&, k]() {
+        int64_t c = 0;
+        for (const char *s = cut[k]; s < cut[k + 1];) {
+          const char *e = (const char *)std::memchr(s, '\n', (size_t)(cut[k + 1] - s));
+          if (!e) e = cut[k + 1];
+          if (is_entry_line(s, e)) ++c;
+          s = e + 1;
+        }
+        cnt[k + 1] = c;
+      });
+    for (auto &x : th) x.join();
+  }
+  for (unsigned k = 0; k < nthr; ++k) cnt[k + 1] += cnt[k];
+  if (cnt[nthr] < NZ) {
+    pf::set_error("pf_mmio_read: file has %lld entries, header says %lld",
+                  (long long)cnt[nthr], NZ);
+    return PF_ERR_FORMAT;
+  }
+  Entries E;
+  E.ri.resize((size_t)NZ);
+  E.ci.resize((size_t)NZ);
+  E.v.resize((size_t)NZ);
+  std::vector<int> bad(nthr, 0);
+  {
+    std::vector<std::thread> th;
+    for (unsigned k = 0; k < nthr; ++k)
+      th.emplace_back([&, k]() {
+        int64_t o = cnt[k];
+        for (const char *s = cut[k]; s < cut[k + 1] && o < NZ;) {
+          const char *e = (const char *)std::memchr(s, '\n', (size_t)(cut[k + 1] - s));
+          if (!e) e = cut[k + 1];
+          if (is_entry_line(s, e)) {
+            int64_t i, j;
+            double v;
+            if (!parse_entry(s, e, nv, is_int, &i, &j, &v) || i < 1 || i > M || j < 1 ||
+                j > N) {
+              bad[k] = 1;
+              return;
+            }
+            E.ri[(size_t)o] = (int32_t)(i - 1);
+            E.ci[(size_t)o] = (int32_t)(j - 1);
+            E.v[(size_t)o] = v;
+            ++o;
+          }
+          s = e + 1;
+        }
+      });
+    for (auto &x : th) x.join();
+  }
+  for (unsigned k = 0; k < nthr; ++k)
+    if (bad[k]) {
+      pf::set_error("pf_mmio_read: malformed entry or index out of range");
+      return PF_ERR_FORMAT;
+    }
+  if (sym && M != N) {
+    pf::set_error("pf_mmio_read: symmetric file with M != N");
+    return PF_ERR_FORMAT;
+  }
+
+  // counting sort in file order
+  int64_t *rp = (int64_t *)std::calloc((size_t)M + 1, sizeof(int64_t));
+  if (!rp) {
+    pf::set_error("pf_mmio_read: out of host memory");
+    return PF_ERR_INVALID;
+  }
+  for (int64_t k = 0; k < NZ; ++k) {
+    rp[E.ri[(size_t)k]]++;
+    if (sym && E.ri[(size_t)k] != E.ci[(size_t)k]) rp[E.ci[(size_t)k]]++;
+  }
+  int64_t run = 0;
+  for (int64_t r = 0; r <= M; ++r) {
+    const int64_t c = rp[r];
+    rp[r] = run;
+    run += c;
+  }
+  const int64_t nnz = run;
+  int32_t *col = (int32_t *)std::malloc(sizeof(int32_t) * (size_t)std::max<int64_t>(nnz, 1));
+  double *val = (double *)std::malloc(sizeof(double) * (size_t)std::max<int64_t>(nnz, 1));
+  std::vector<int64_t> cur(rp, rp + M);
+  if (!col || !val) {
+    std::free(rp);
+    std::free(col);
+    std::free(val);
+    pf::set_error("pf_mmio_read: out of host memory");
+    return PF_ERR_INVALID;
+  }
+  for (int64_t k = 0; k < NZ; ++k) {
+    const int32_t i = E.ri[(size_t)k], j = E.ci[(size_t)k];
+    const double v = E.v[(size_t)k];
+    int64_t o = cur[(size_t)i]++;
+    col[o] = j;
+    val[o] = v;
+    if (sym && i != j) {
+      o = cur[(size_t)j]++;
+      col[o] = i;
+      val[o] = v;
+    }
+  }
+  *m_out = M;
+  *n_out = N;
+  *nnz_out = nnz;
+  *sym_out = sym ? 1 : 0;
+  *row_ptr_out = rp;
+  *col_out = col;
+  *val_out = val;
+  return PF_OK;
+}
+
+pf_status pf_shard_bounds_i32(const int32_t *row_ptr, int64_t m, int parts, int64_t *bounds) {
+  return shard_bounds(row_ptr, m, parts, bounds);
+}
+pf_status pf_shard_bounds_i64(const int64_t *row_ptr, int64_t m, int parts, int64_t *bounds) {
+  return shard_bounds(row_ptr, m, parts, bounds);
+}
+
+}  // extern "C"

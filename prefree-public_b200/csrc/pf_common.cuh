@@ -1,0 +1,48 @@
+// Common definitions for the B200 CSR SpMV library: status handling, launch
+// bookkeeping and small device helpers shared by the kernels.
+#pragma once
+
+#include <cstdint>
+#include <cstdio>
+#include <cuda_runtime.h>
+
+#include "../../include/prefree_b200.h"
+
+namespace pf {
+
+// Per-thread last-error text, returned by pf_last_error().
+void set_error(const char *fmt, ...);
+
+#define PF_CUDA_TRY(call)                                                      \
+  do {                                                                         \
+    cudaError_t e_ = (call);                                                   \
+    if (e_ != cudaSuccess) {                                                   \
+      ::pf::set_error("%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_),  \
+                      __FILE__, __LINE__);                                     \
+      return PF_ERR_CUDA;                                                      \
+    }                                                                          \
+  } while (0)
+
+#define PF_CHECK_ARG(cond, ...)                                                \
+  do {                                                                         \
+    if (!(cond)) {                                                             \
+      ::pf::set_error(__VA_ARGS__);                                            \
+      return PF_ERR_INVALID;                                                   \
+    }                                                                          \
+  } while (0)
+
+// Device-side error bits (written into the handle's error word; never trap).
+enum : unsigned {
+  PF_DEVERR_WAIT_TIMEOUT = 1u << 0,   // a bounded mbarrier/flag wait gave up
+  PF_DEVERR_BOUNDS = 1u << 1,         // a row_ptr/col index outside its range
+  PF_DEVERR_ROWPTR = 1u << 2,         // row_ptr not non-decreasing
+};
+
+// Count of our kernels launched since library load (bench reports it).
+extern unsigned long long g_launch_count;
+
+__host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) {
+  return (a + b - 1) / b;
+}
+
+}  // namespace pf
