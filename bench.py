@@ -1,0 +1,366 @@
+#!/usr/bin/env python
+"""Benchmark: CSR SpMV GFLOP/s (2*nnz/t) on B200, config 5 of the baseline.
+
+Workload (the largest config; it fits one GPU):
+64M x 64M CSR, 32 nnz/row (2^31 non-zeros), int64 row_ptr, int32 col, fp64,
+70% of columns within +-4096 of the diagonal, 30% uniform; seeded synthetic
+data (counter-based generator, seed 12345). One step = one iterated multiply
+y <- A*y/||y||: the local SpMV on each rank's equal-nnz row shard, an 8-byte
+all-reduce of ||y||^2 and an all-gather of y into every rank's x (NCCL).
+`scaling` is "strong": the matrix is fixed, N GPUs share it.
+
+Timing: W warm-up steps, then K steps between barrier + synchronize, CUDA
+events on the compute stream, max over ranks. Inputs (27 GB) are far larger
+than L2 (126 MB), so no flush is needed between steps.
+
+`--impl reference` times the reference's own CPU SpMV (spmv_serial of
+test/test_cdspmv.cpp:4-20, compiled from the reference sources into
+oracle/_ref/libref.so) on a bounded row sample of the same workload, with
+every host thread (row slices in parallel); rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import importlib
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "SpMV GFLOP/s (2*nnz/t) and achieved HBM GB/s vs roofline"
+WORKLOAD = "config5: 64Mx64M CSR, 32 nnz/row (2^31 nnz), int64 row_ptr, fp64, 70% band +-4096 / 30% uniform cols; 10-step power iteration y<-A*y/||y||"
+SEED = 12345
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d.get("hbm_gbs", 6650.0)), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def traffic_per_row():
+    """DRAM bytes per row of the config-5 kernel from the committed ncu capture
+    (profiles/config5_spmv_traffic.json), or None."""
+    p = os.path.join(ROOT, "profiles", "config5_spmv_traffic.json")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        return json.load(f).get("dram_bytes_per_row")
+
+
+def cpu_reference_sample(pf, oracle, spec, rows: int, threads: int):
+    """Host CSR sample (rows [0, rows)) of the workload + full x, generated on
+    the host (library generator, parallel row ranges)."""
+    s = spec.resolved()
+    x = np.zeros(s.n, dtype=np.float64)
+    rp = np.zeros(rows + 1, dtype=np.int64)
+    z = pf.gen_count(spec, 0, rows)
+    col = np.zeros(z, dtype=np.int32)
+    val = np.zeros(z, dtype=np.float64)
+    cs = s.c()
+    cuts = [rows * k // threads for k in range(threads + 1)]
+    xc = [s.n * k // threads for k in range(threads + 1)]
+
+    def work(k):
+        r0, r1 = cuts[k], cuts[k + 1]
+        o0 = pf.gen_count(spec, 0, r0)
+        lrp = np.zeros(r1 - r0 + 1, dtype=np.int64)
+        pf._check(pf.lib.pf_gen_rows_host(C.byref(cs), r0, r1, lrp.ctypes.data,
+                                          col.ctypes.data + 4 * o0, val.ctypes.data + 8 * o0))
+        rp[r0 + 1:r1 + 1] = lrp[1:] + o0
+        pf._check(pf.lib.pf_gen_x_host(C.byref(cs), xc[k], xc[k + 1], x.ctypes.data + 8 * xc[k]))
+
+    ts = [threading.Thread(target=work, args=(k,)) for k in range(threads)]
+    [t.start() for t in ts]
+    [t.join() for t in ts]
+    return rp, col, val, x
+
+
+def run_reference(args, rank):
+    """--impl reference: the reference's CPU spmv_serial on all host threads."""
+    if rank != 0:
+        return
+    pf = importlib.import_module("prefree-public_b200")
+    import oracle
+    threads = os.cpu_count() or 1
+    spec = pf.GenSpec(cfg=5, seed=SEED)
+    rows = 1 << 23                      # 2^28 non-zeros per sampled step
+    rp, col, val, x = cpu_reference_sample(pf, oracle, spec, rows, threads)
+    rp32 = rp.astype(np.int32)
+    kind = "reference" if oracle.ref_available() else "port"
+
+    def one():
+        if kind == "reference":
+            return oracle.ref_serial_threaded(rp32, col, val, x, threads)
+        return oracle.serial(rp, col, val, x)
+
+    for _ in range(args.warmup):
+        one()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one()
+    dt = (time.perf_counter() - t0) / args.steps
+    z = int(rp[-1])
+    v = 2.0 * z / dt / 1e9
+    sample = (f"rows [0, 2^23) of config 5 ({z} nnz, x of 2^26) per step; "
+              f"spmv_serial on {threads} equal-nnz row slices in parallel threads")
+    print(json.dumps({
+        "metric": METRIC, "value": v, "unit": "GFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (seeded generator)", "impl": "reference",
+        "config": {"workload": WORKLOAD, "parallelism": "host threads", "sample_rows": rows},
+        "cpu_baseline": {"value": v, "unit": "GFLOP/s", "cores": threads, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": v, "unit": "GFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    assert args.warmup >= 3 or args.impl == "reference" or os.environ.get("PF_BENCH_ALLOW_SHORT"), \
+        "at least 3 warm-up steps"
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=dev)
+    pf = importlib.import_module("prefree-public_b200")
+    pfd = importlib.import_module("prefree-public_b200.dist")
+
+    spec = pf.GenSpec(cfg=5, seed=SEED).resolved()
+    bounds = pfd.gen_bounds(pf, spec, world)
+    r0, r1 = int(bounds[rank]), int(bounds[rank + 1])
+    m_loc, n = r1 - r0, spec.n
+    rp, col, val = pf.gen_rows_device(spec, r0, r1, index_dtype=torch.int64,
+                                      value_dtype=torch.float64, device=dev)
+    x = pf.gen_x_device(spec, value_dtype=torch.float64, device=dev)
+    y = torch.empty(m_loc, dtype=torch.float64, device=dev)
+    nnz_loc = col.numel()
+    z_tot = torch.tensor([nnz_loc], dtype=torch.int64, device=dev)
+    if world > 1:
+        dist.all_reduce(z_tot)
+    z_tot = int(z_tot.item())
+    h = pf.Handle()
+    stream = torch.cuda.current_stream(dev)
+    ev_pairs = []
+
+    def local_spmv(xf, yl, alpha):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        pf.spmv(h, m_loc, n, nnz_loc, rp, col, val, xf, yl, alpha, 0.0, stream=stream)
+        e1.record(stream)
+        ev_pairs.append((e0, e1))
+
+    it = pfd.PowerIteration(local_spmv, x, y, bounds, rank, world)
+    for _ in range(args.warmup):
+        it.step()
+    torch.cuda.synchronize()
+    ev_pairs.clear()
+
+    # ---- timed region ------------------------------------------------------------
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = pf.launch_count()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        t_start.record(stream)
+        for _ in range(args.steps):
+            st = it.step()
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    launches = pf.launch_count() - launches0
+    step_ms = t_start.elapsed_time(t_end) / args.steps
+    kern_ms = sum(a.elapsed_time(b) for a, b in ev_pairs) / len(ev_pairs)
+    stats = torch.tensor([step_ms, kern_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    step_ms, kern_ms = float(stats[0]), float(stats[1])
+    assert h.device_error() == 0, "device error word set"
+    final_norm = math.sqrt(st.norm_sq)
+
+    # roofline of the SpMV kernel (rank with the slowest launch)
+    alg_bytes = pf.compulsory_bytes(m_loc, n, nnz_loc, 8, 8)
+    hbm_peak, peak_src = peaks()
+    achieved = alg_bytes / (kern_ms * 1e-3) / 1e9
+    tpr = traffic_per_row()
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                "frac": achieved / hbm_peak, "peak_source": peak_src,
+                "traffic": (tpr * m_loc) if tpr else None,
+                "algorithmic_bytes_per_launch": alg_bytes, "kernel_ms": kern_ms}
+
+    # ---- e2e: the host-buffer C-ABI call, copies inside the timed region ----------
+    e2e = None
+    if not args.no_e2e:
+        ks = args.e2e_steps or max(1, min(args.steps, 5))
+        h_rp = torch.empty(rp.shape, dtype=torch.int64, pin_memory=True)
+        h_col = torch.empty(col.shape, dtype=torch.int32, pin_memory=True)
+        h_val = torch.empty(val.shape, dtype=torch.float64, pin_memory=True)
+        h_x = torch.empty(x.shape, dtype=torch.float64, pin_memory=True)
+        h_y = torch.empty(y.shape, dtype=torch.float64, pin_memory=True)
+        h_rp.copy_(rp)
+        h_col.copy_(col)
+        h_val.copy_(val)
+        h_x.copy_(x)
+        he = pf.Handle()
+        a_rp, a_col, a_val, a_x, a_y = (t.numpy() for t in (h_rp, h_col, h_val, h_x, h_y))
+        pf.spmv_host(he, a_rp, a_col, a_val, a_x, a_y, stream=stream.cuda_stream)  # warm-up
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(ks):
+            pf.spmv_host(he, a_rp, a_col, a_val, a_x, a_y, stream=stream.cuda_stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = torch.tensor([e0.elapsed_time(e1) / ks], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        h2d = torch.tensor([h_rp.numel() * 8 + h_col.numel() * 4 + h_val.numel() * 8 +
+                            h_x.numel() * 8, h_y.numel() * 8], dtype=torch.int64, device=dev)
+        if world > 1:
+            dist.all_reduce(h2d)
+        e2e = {"value": 2.0 * z_tot / (float(e_ms) * 1e-3) / 1e9, "unit": "GFLOP/s",
+               "h2d_bytes_per_step": int(h2d[0]), "d2h_bytes_per_step": int(h2d[1]),
+               "ms_per_step": float(e_ms), "steps": ks,
+               "call": "pf_spmv_host_f64_i64 per rank on its host shard (one multiply)"}
+        he.close()
+        del h_rp, h_col, h_val, h_x, h_y
+
+    # ---- CPU baseline (rank 0, N = 1): the reference's spmv_serial, 1 thread -------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        import oracle
+        rows = 1 << 21
+        hrp = rp[:rows + 1].cpu().numpy()
+        zc = int(hrp[-1])
+        hcol = col[:zc].cpu().numpy()
+        hval = val[:zc].cpu().numpy()
+        x0 = pf.gen_x_device(spec, value_dtype=torch.float64, device=dev).cpu().numpy()
+        kind = "reference" if oracle.ref_available() else "port"
+        t0 = time.perf_counter()
+        if kind == "reference":
+            oracle.ref_serial(hrp.astype(np.int32), hcol, hval, x0)
+        else:
+            oracle.serial(hrp, hcol, hval, x0)
+        dt = time.perf_counter() - t0
+        cpu = {"value": 2.0 * zc / dt / 1e9, "unit": "GFLOP/s", "cores": 1, "kind": kind,
+               "sample": f"rows [0, 2^21) of config 5 ({zc} nnz), one multiply, single thread "
+                         "(spmv_serial is serial by construction)"}
+
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": 2.0 * z_tot / (step_ms * 1e-3) / 1e9, "unit": "GFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (seeded counter-based generator; SuiteSparse files are not available)",
+            "config": {"workload": WORKLOAD, "m": spec.m, "n": spec.n, "nnz": z_tot,
+                       "index": "int64 row_ptr, int32 col", "parallelism": f"row shards x{world}",
+                       "l2": "inputs (27 GB) larger than L2: no flush",
+                       "step": "local SpMV + all-reduce ||y||^2 + all-gather y"},
+            "gpu_launches": int(launches),
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "clocks": clocks.summary(),
+            "check": {"final_norm_sq_of_y": st.norm_sq, "final_norm": final_norm},
+        }
+        print(json.dumps(out), flush=True)
+    h.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

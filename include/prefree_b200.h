@@ -44,7 +44,9 @@ typedef enum pf_status {
 typedef enum pf_variant {
   PF_VARIANT_AUTO = 0,
   PF_VARIANT_NNZSPLIT = 1, /* nnz-balanced CTA slices, any row length        */
-  PF_VARIANT_ROWGROUP = 2  /* row-aligned slices, warp lanes per row (short) */
+  PF_VARIANT_ROWGROUP = 2, /* row-aligned slices, warp lanes per row (short) */
+  PF_VARIANT_NNZSPLIT_LDG = 3, /* NNZSPLIT with plain coalesced loads (no TMA) */
+  PF_VARIANT_ROWVEC = 4    /* row-aligned, 16-byte block loads per lane        */
 } pf_variant;
 
 typedef struct pf_handle_s *pf_handle;

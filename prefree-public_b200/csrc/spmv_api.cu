@@ -9,6 +9,9 @@
 
 #include "pf_common.cuh"
 #include "spmv_nnzsplit.cuh"
+#include "spmv_rowgroup.cuh"
+#include "spmv_rowvec.cuh"
+#include "spmv_tma.cuh"
 
 namespace pf {
 
@@ -34,10 +37,28 @@ static void count_launch(unsigned long long k = 1) {
 
 // Per-device state: scratch for cut-row carries, error word, cached buffers
 // for the host-buffer entry points.
+struct pf_variant_choice {
+  int variant;  // PF_VARIANT_NNZSPLIT / ROWGROUP / NNZSPLIT_LDG
+  int lanes;    // ROWGROUP lanes per row
+};
+
+struct pf_select_entry {
+  const void *row_ptr;
+  int64_t m, nnz;
+  int idx_bytes;
+  pf_variant_choice choice;
+};
+
 struct pf_handle_s {
   int device = 0;
   int num_sms = 0;
   int variant = PF_VARIANT_AUTO;
+  // selector cache: decision per (row_ptr, m, nnz); any variant is correct
+  // for any matrix, so a stale entry can only cost speed
+  pf_select_entry cache[16];
+  int cache_n = 0, cache_next = 0;
+  int64_t *sample_dev = nullptr;
+  int64_t *sample_host = nullptr;  // pinned
   int64_t slice_override = 0;  // testing knob: fixed nnz per CTA slice
   // cut-row scratch
   double *carry = nullptr;     // 2 * cap doubles (head, tail)
@@ -93,6 +114,124 @@ static int nnzsplit_occupancy() {
 }
 
 template <typename VT, typename IT>
+static int tma_occupancy(size_t *smem_out) {
+  using C = TmaCfgDefault;
+  static int occ = -1;
+  const size_t smem = sizeof(TmaSmem<VT, IT, C>);
+  if (occ < 0) {
+    cudaFuncSetAttribute(spmv_tma_kernel<VT, IT, C>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    int o = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, spmv_tma_kernel<VT, IT, C>, C::NT, smem);
+    occ = std::max(1, o);
+  }
+  *smem_out = smem;
+  return occ;
+}
+
+// ---- variant selection from sampled row lengths ------------------------------
+static int rowgroup_lanes(double avg) {
+  int v = 4;
+  while (v < 32 && v < avg) v *= 2;
+  return v;
+}
+
+// ROWVEC lanes: one 4-element block per lane covers an average row
+static int rowvec_lanes(double avg) {
+  int v = 2;
+  while (v < 32 && 4 * v < avg) v *= 2;
+  return v;
+}
+
+constexpr int kSampleRows = 1024;
+
+template <typename IT>
+__global__ void sample_lengths_kernel(const IT *row_ptr, int64_t m, int S, int64_t *out) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < S; i += gridDim.x * blockDim.x) {
+    const int64_t r = (int64_t)((__int128)m * (2 * i + 1) / (2 * S));
+    out[i] = (int64_t)row_ptr[r + 1] - (int64_t)row_ptr[r];
+  }
+}
+
+static pf_variant_choice choose_from_stats(int64_t m, int64_t nnz, int64_t sample_max) {
+  const double avg = m > 0 ? (double)nnz / (double)m : 0.0;
+  pf_variant_choice ch;
+  // regular rows (the sample never strays far above the mean): whole rows per
+  // lane group; otherwise nnz-balanced slices
+  if (sample_max <= 4.0 * avg + 32.0) {
+    ch.variant = PF_VARIANT_ROWVEC;
+    ch.lanes = rowvec_lanes(avg);
+  } else {
+    ch.variant = PF_VARIANT_NNZSPLIT;
+    ch.lanes = 32;
+  }
+  return ch;
+}
+
+template <typename IT>
+static pf_status select_variant(pf_handle h, int64_t m, int64_t nnz, const IT *row_ptr,
+                                cudaStream_t st, pf_variant_choice *out) {
+  if (h->variant != PF_VARIANT_AUTO) {
+    const double avg = m > 0 ? (double)nnz / (double)m : 0.0;
+    *out = pf_variant_choice{h->variant, h->variant == PF_VARIANT_ROWVEC ? rowvec_lanes(avg)
+                                                                         : rowgroup_lanes(avg)};
+    return PF_OK;
+  }
+  for (int i = 0; i < h->cache_n; ++i) {
+    const pf_select_entry &c = h->cache[i];
+    if (c.row_ptr == row_ptr && c.m == m && c.nnz == nnz && c.idx_bytes == (int)sizeof(IT)) {
+      *out = c.choice;
+      return PF_OK;
+    }
+  }
+  if (!h->sample_dev) {
+    PF_CUDA_TRY(cudaMalloc(&h->sample_dev, sizeof(int64_t) * kSampleRows));
+    PF_CUDA_TRY(cudaMallocHost(&h->sample_host, sizeof(int64_t) * kSampleRows));
+  }
+  const int S = (int)std::min<int64_t>(m, kSampleRows);
+  sample_lengths_kernel<IT><<<(S + 255) / 256, 256, 0, st>>>(row_ptr, m, S, h->sample_dev);
+  count_launch();
+  PF_CUDA_TRY(cudaGetLastError());
+  PF_CUDA_TRY(cudaMemcpyAsync(h->sample_host, h->sample_dev, sizeof(int64_t) * S,
+                              cudaMemcpyDeviceToHost, st));
+  PF_CUDA_TRY(cudaStreamSynchronize(st));
+  int64_t mx = 0;
+  for (int i = 0; i < S; ++i) mx = std::max(mx, h->sample_host[i]);
+  *out = choose_from_stats(m, nnz, mx);
+  pf_select_entry &c = h->cache[h->cache_next];
+  c = pf_select_entry{row_ptr, m, nnz, (int)sizeof(IT), *out};
+  h->cache_next = (h->cache_next + 1) % 16;
+  h->cache_n = std::min(16, h->cache_n + 1);
+  return PF_OK;
+}
+
+template <typename VT, typename IT, int V>
+static pf_status launch_rowgroup(pf_handle h, const SpmvParams<VT, IT> &prm, cudaStream_t st) {
+  constexpr int U = 4, NTB = 256;
+  const int64_t rows_per_block = (int64_t)(NTB / 32) * (32 / V) * U;
+  const int64_t want = ceil_div(prm.m, rows_per_block);
+  const int64_t cap = (int64_t)h->num_sms * 32;
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min(want, cap));
+  spmv_rowgroup_kernel<VT, IT, V, U, NTB><<<grid, NTB, 0, st>>>(prm);
+  count_launch();
+  PF_CUDA_TRY(cudaGetLastError());
+  return PF_OK;
+}
+
+template <typename VT, typename IT, int V>
+static pf_status launch_rowvec(pf_handle h, const SpmvParams<VT, IT> &prm, cudaStream_t st) {
+  constexpr int U = 2, NTB = 256;
+  const int64_t rows_per_block = (int64_t)(NTB / 32) * (32 / V) * U;
+  const int64_t want = ceil_div(prm.m, rows_per_block);
+  const int64_t cap = (int64_t)h->num_sms * 16;
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min(want, cap));
+  spmv_rowvec_kernel<VT, IT, V, U, NTB><<<grid, NTB, 0, st>>>(prm);
+  count_launch();
+  PF_CUDA_TRY(cudaGetLastError());
+  return PF_OK;
+}
+
+template <typename VT, typename IT>
 static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
                              const IT *row_ptr, const int32_t *col,
                              const VT *val, double alpha, const VT *x,
@@ -105,6 +244,12 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
   PF_CHECK_ARG(nnz == 0 || (col && val && x), "null col/val/x with nnz > 0");
   PF_CHECK_ARG(sizeof(IT) == 8 || nnz <= INT32_MAX, "int32 row_ptr cannot index nnz=%lld",
                (long long)nnz);
+  PF_CHECK_ARG(n <= (int64_t)INT32_MAX + 1, "n must fit int32 column indices");
+  PF_CHECK_ARG(nnz == 0 || n > 0, "nnz > 0 needs n > 0 (column indices lie in [0, n))");
+  PF_CHECK_ARG(((uintptr_t)row_ptr % sizeof(IT)) == 0 && ((uintptr_t)y % sizeof(VT)) == 0 &&
+                   (nnz == 0 || (((uintptr_t)col % 4) == 0 && ((uintptr_t)val % sizeof(VT)) == 0 &&
+                                 ((uintptr_t)x % sizeof(VT)) == 0)),
+               "arrays must be aligned to their element size");
   int cur = 0;
   PF_CUDA_TRY(cudaGetDevice(&cur));
   PF_CHECK_ARG(cur == h->device, "handle bound to device %d, current device is %d",
@@ -119,26 +264,14 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
     return PF_OK;
   }
 
-  using C = NnzSplitCfg<VT, IT>;
-  constexpr int TILE = C::NT * C::K;
-  int64_t T;
-  if (h->slice_override > 0) {
-    T = h->slice_override;
-  } else {
-    const int64_t ctas = (int64_t)h->num_sms * nnzsplit_occupancy<VT, IT>();
-    T = std::max<int64_t>(ceil_div(nnz, ctas), TILE);
-  }
-  const int64_t P = ceil_div(nnz, T);
-  PF_CHECK_ARG(P <= INT32_MAX, "too many CTA slices");
-  pf_status s = ensure_scratch(h, P, st);
+  pf_variant_choice ch;
+  pf_status s = select_variant<IT>(h, m, nnz, row_ptr, st, &ch);
   if (s != PF_OK) return s;
 
   SpmvParams<VT, IT> prm;
   prm.m = m;
   prm.n = n;
   prm.nnz = nnz;
-  prm.T = T;
-  prm.num_ctas = P;
   prm.row_ptr = row_ptr;
   prm.col = col;
   prm.val = val;
@@ -146,11 +279,73 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
   prm.y = y;
   prm.alpha = alpha;
   prm.beta = beta;
+  prm.err = h->err;
+
+  // ROWVEC needs 16-byte aligned col/val (16-byte block loads)
+  if (ch.variant == PF_VARIANT_ROWVEC &&
+      (((uintptr_t)col | (uintptr_t)val) & 15) != 0) {
+    ch.variant = PF_VARIANT_ROWGROUP;
+    ch.lanes = rowgroup_lanes(m > 0 ? (double)nnz / (double)m : 0.0);
+  }
+  if (ch.variant == PF_VARIANT_ROWVEC) {
+    prm.T = 0;
+    prm.num_ctas = 0;
+    prm.carry_head = prm.carry_tail = nullptr;
+    prm.counters = nullptr;
+    switch (ch.lanes) {
+      case 2: return launch_rowvec<VT, IT, 2>(h, prm, st);
+      case 4: return launch_rowvec<VT, IT, 4>(h, prm, st);
+      case 8: return launch_rowvec<VT, IT, 8>(h, prm, st);
+      case 16: return launch_rowvec<VT, IT, 16>(h, prm, st);
+      default: return launch_rowvec<VT, IT, 32>(h, prm, st);
+    }
+  }
+  if (ch.variant == PF_VARIANT_ROWGROUP) {
+    prm.T = 0;
+    prm.num_ctas = 0;
+    prm.carry_head = prm.carry_tail = nullptr;
+    prm.counters = nullptr;
+    switch (ch.lanes) {
+      case 4: return launch_rowgroup<VT, IT, 4>(h, prm, st);
+      case 8: return launch_rowgroup<VT, IT, 8>(h, prm, st);
+      case 16: return launch_rowgroup<VT, IT, 16>(h, prm, st);
+      default: return launch_rowgroup<VT, IT, 32>(h, prm, st);
+    }
+  }
+
+  const bool tma = (ch.variant == PF_VARIANT_NNZSPLIT);
+  size_t smem = 0;
+  int64_t T, min_T;
+  int occ;
+  if (tma) {
+    occ = tma_occupancy<VT, IT>(&smem);
+    min_T = 2 * TmaCfgDefault::TILE;
+  } else {
+    occ = nnzsplit_occupancy<VT, IT>();
+    min_T = NnzSplitCfg<VT, IT>::NT * NnzSplitCfg<VT, IT>::K;
+  }
+  if (h->slice_override > 0) {
+    T = h->slice_override;
+  } else {
+    const int64_t ctas = (int64_t)h->num_sms * occ;
+    T = std::max<int64_t>(ceil_div(nnz, ctas), min_T);
+  }
+  const int64_t P = ceil_div(nnz, T);
+  PF_CHECK_ARG(P <= INT32_MAX, "too many CTA slices");
+  s = ensure_scratch(h, P, st);
+  if (s != PF_OK) return s;
+  prm.T = T;
+  prm.num_ctas = P;
   prm.carry_head = h->carry;
   prm.carry_tail = h->carry + h->cap;
   prm.counters = h->counters;
-  prm.err = h->err;
-  spmv_nnzsplit_kernel<VT, IT, C::NT, C::K, C::W><<<(unsigned)P, C::NT, 0, st>>>(prm);
+  if (tma) {
+    using C = TmaCfgDefault;
+    spmv_tma_kernel<VT, IT, C><<<(unsigned)P, C::NT, smem, st>>>(prm);
+  } else {
+    using C = NnzSplitCfg<VT, IT>;
+    spmv_nnzsplit_kernel<VT, IT, C::NT, C::K, C::W><<<(unsigned)P, C::NT, 0, st>>>(prm);
+  }
   count_launch();
   PF_CUDA_TRY(cudaGetLastError());
   return PF_OK;
@@ -245,6 +440,8 @@ pf_status pf_handle_destroy(pf_handle h) {
   if (h->err) cudaFree(h->err);
   for (int i = 0; i < 5; ++i)
     if (h->hbuf[i]) cudaFree(h->hbuf[i]);
+  if (h->sample_dev) cudaFree(h->sample_dev);
+  if (h->sample_host) cudaFreeHost(h->sample_host);
   cudaSetDevice(cur);
   delete h;
   return PF_OK;
@@ -252,7 +449,7 @@ pf_status pf_handle_destroy(pf_handle h) {
 
 pf_status pf_handle_set_variant(pf_handle h, int variant) {
   PF_CHECK_ARG(h != nullptr, "null handle");
-  PF_CHECK_ARG(variant >= PF_VARIANT_AUTO && variant <= PF_VARIANT_ROWGROUP,
+  PF_CHECK_ARG(variant >= PF_VARIANT_AUTO && variant <= PF_VARIANT_ROWVEC,
                "unknown variant %d", variant);
   h->variant = variant;
   return PF_OK;

@@ -1,0 +1,99 @@
+"""Row-sharded multi-GPU SpMV: one process per GPU, torch.distributed (NCCL)
+for the plumbing.
+
+Layout (no counterpart in the reference, which is single-GPU):
+  * rows are split at equal-nnz boundaries (``shard_bounds``); rank k owns
+    rows [b_k, b_{k+1}) with its own CSR slice (row_ptr rebased to 0), a full
+    replica of x, and writes the disjoint slice y[b_k, b_{k+1});
+  * a single multiply needs no collective (each rank's y slice is final);
+  * the iterated multiply y <- A*y/||y|| (benchmark config 5) re-assembles y
+    into every rank's next x with an all-gather over NVLink and reduces the
+    8-byte partial ||y||^2 with an all-reduce.
+
+The local multiply is the library's CUDA kernel on the rank's slice; the
+iteration logic here is written against a ``local_spmv`` callable and a
+process group so that the same code runs on CPU ``gloo`` ranks in the tests.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+
+
+def equal_nnz_bounds(row_lengths_prefix: np.ndarray, parts: int) -> np.ndarray:
+    """bounds[k] = first row r with prefix[r] >= k*nnz/parts (prefix = row_ptr)."""
+    rp = np.asarray(row_lengths_prefix, dtype=np.int64)
+    m = len(rp) - 1
+    z = int(rp[-1] - rp[0])
+    b = np.zeros(parts + 1, dtype=np.int64)
+    for k in range(1, parts):
+        b[k] = max(int(np.searchsorted(rp, int(rp[0]) + (z * k) // parts, side="left")), b[k - 1])
+    b[parts] = m
+    return b
+
+
+def gen_bounds(pf, spec, parts: int) -> np.ndarray:
+    """Equal-nnz row bounds of a generated config without materialising it:
+    fixed-length configs split by rows; others through the row-length prefix."""
+    s = spec.resolved()
+    if s.cfg in (1, 4, 5):
+        return np.array([(s.m * k) // parts for k in range(parts + 1)], dtype=np.int64)
+    lens = np.zeros(s.m, dtype=np.int64)
+    import ctypes as C
+    pf._check(pf.lib.pf_gen_row_lengths_host(C.byref(s.c()), 0, s.m, lens.ctypes.data))
+    rp = np.zeros(s.m + 1, dtype=np.int64)
+    np.cumsum(lens, out=rp[1:])
+    return equal_nnz_bounds(rp, parts)
+
+
+@dataclass
+class StepStats:
+    norm_sq: float
+
+
+class PowerIteration:
+    """x_{k+1} = A x_k / ||A x_k|| over row shards.
+
+    ``local_spmv(x_full, y_local, alpha)`` computes y_local = alpha * A_k x_full
+    for this rank's rows. ``x`` holds the previous (unnormalised) iterate on
+    every rank, and the normalisation 1/||x|| is applied as the next multiply's
+    alpha, so no extra pass over x is needed.
+    """
+
+    def __init__(self, local_spmv, x_full, y_local, bounds, rank: int, world: int,
+                 group=None, torch_mod=None):
+        import torch
+        import torch.distributed as dist
+        self.torch = torch_mod or torch
+        self.dist = dist
+        self.local_spmv = local_spmv
+        self.x = x_full
+        self.y = y_local
+        self.bounds = bounds
+        self.rank, self.world, self.group = rank, world, group
+        self.equal = len(set(int(bounds[k + 1] - bounds[k]) for k in range(world))) == 1
+        # 1/||x0||
+        nsq = float(self.torch.dot(x_full, x_full).item())
+        self.alpha = 1.0 / math.sqrt(nsq) if nsq > 0 else 1.0
+
+    def step(self) -> StepStats:
+        torch, dist = self.torch, self.dist
+        self.local_spmv(self.x, self.y, self.alpha)
+        sq = torch.dot(self.y, self.y).reshape(1)
+        if self.world > 1:
+            dist.all_reduce(sq, group=self.group)
+            if self.equal and dist.get_backend(self.group) == "nccl":
+                dist.all_gather_into_tensor(self.x, self.y, group=self.group)
+            else:
+                # all-gather-v: each rank broadcasts its slice of y into x
+                b = self.bounds
+                self.x[int(b[self.rank]):int(b[self.rank + 1])].copy_(self.y)
+                for k in range(self.world):
+                    dist.broadcast(self.x[int(b[k]):int(b[k + 1])], src=k, group=self.group)
+        else:
+            self.x.copy_(self.y)
+        nsq = float(sq.item())
+        self.alpha = 1.0 / math.sqrt(nsq) if nsq > 0 else 1.0
+        return StepStats(nsq)

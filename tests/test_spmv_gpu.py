@@ -71,27 +71,63 @@ def check(oracle, y, rp, col, val, x, vdt, alpha=1.0, beta=0.0, y0=None):
     assert ok, f"{nbad} rows out of tolerance (worst ratio {worst:.3g})"
 
 
+VARIANTS = {"auto": 0, "nnzsplit": 1, "rowgroup": 2, "nnzsplit_ldg": 3, "rowvec": 4}
+
+
+@pytest.fixture
+def variant_handle(handle, request):
+    handle.set_variant(VARIANTS[request.param])
+    yield handle
+    handle.set_variant(0)
+    handle.set_slice(0)
+
+
+@pytest.mark.parametrize("variant_handle", list(VARIANTS), indirect=True)
 @pytest.mark.parametrize("name", CASES)
 @pytest.mark.parametrize("vdt", [np.float64, np.float32])
 @pytest.mark.parametrize("idt", [np.int32, np.int64])
-def test_cases_auto(pf, oracle, torch_cuda, handle, name, vdt, idt):
+def test_cases_variants(pf, oracle, torch_cuda, variant_handle, name, vdt, idt):
     rp, col, val, n = case(name, seed=1)
     x = np.random.default_rng(2).uniform(-1, 1, n)
-    y = run_gpu(pf, torch_cuda, handle, rp, col, val, x, n, vdt, idt)
+    y = run_gpu(pf, torch_cuda, variant_handle, rp, col, val, x, n, vdt, idt)
     check(oracle, y, rp, col, val, x, vdt)
 
 
+@pytest.mark.parametrize("variant_handle", ["nnzsplit", "nnzsplit_ldg"], indirect=True)
 @pytest.mark.parametrize("name", ["tiny", "row0_long", "empty_edges", "powerlaw", "mixed_long"])
 @pytest.mark.parametrize("slice_nnz", [1, 3, 7, 64, 1000, 5000])
-def test_small_slices_force_cut_rows(pf, oracle, torch_cuda, handle, name, slice_nnz):
+@pytest.mark.parametrize("idt", [np.int32, np.int64])
+def test_small_slices_force_cut_rows(pf, oracle, torch_cuda, variant_handle, name, slice_nnz, idt):
     rp, col, val, n = case(name, seed=3)
     x = np.random.default_rng(4).uniform(-1, 1, n)
-    handle.set_slice(slice_nnz)
-    try:
-        y = run_gpu(pf, torch_cuda, handle, rp, col, val, x, n, np.float64, np.int32)
-    finally:
-        handle.set_slice(0)
+    variant_handle.set_slice(slice_nnz)
+    y = run_gpu(pf, torch_cuda, variant_handle, rp, col, val, x, n, np.float64, idt)
     check(oracle, y, rp, col, val, x, np.float64)
+
+
+@pytest.mark.parametrize("variant_handle", ["nnzsplit", "rowgroup", "rowvec"], indirect=True)
+@pytest.mark.parametrize("offset", [1, 2, 3, 5])
+def test_unaligned_array_starts(pf, oracle, torch_cuda, variant_handle, offset):
+    """val/col/row_ptr that do not start on a 16-byte boundary (views into
+    larger buffers): the bulk copies must round to 16-byte blocks correctly."""
+    torch = torch_cuda
+    rp, col, val, n = case("powerlaw", seed=21)
+    x = np.random.default_rng(22).uniform(-1, 1, n)
+    big_col = torch.zeros(len(col) + 8, dtype=torch.int32, device="cuda")
+    big_val = torch.zeros(len(val) + 8, dtype=torch.float64, device="cuda")
+    big_rp = torch.zeros(len(rp) + 8, dtype=torch.int32, device="cuda")
+    d_col = big_col[offset:offset + len(col)]
+    d_val = big_val[offset:offset + len(val)]
+    d_rp = big_rp[offset:offset + len(rp)]
+    d_col.copy_(torch.from_numpy(col))
+    d_val.copy_(torch.from_numpy(val))
+    d_rp.copy_(torch.from_numpy(rp.astype(np.int32)))
+    d_y = torch.zeros(len(rp) - 1, dtype=torch.float64, device="cuda")
+    variant_handle.set_slice(997)
+    pf.spmv(variant_handle, len(rp) - 1, n, len(col), d_rp, d_col, d_val, to_dev(torch, x), d_y)
+    torch.cuda.synchronize()
+    assert variant_handle.device_error() == 0
+    check(oracle, d_y.cpu().numpy(), rp, col, val, x, np.float64)
 
 
 @pytest.mark.parametrize("alpha,beta", [(2.5, 0.0), (1.0, 1.0), (-0.75, 0.5), (0.0, 2.0)])
