@@ -1,0 +1,78 @@
+"""The C-ABI library: loads, exports every symbol include/*.h declares (and
+the C++ drop-in symbols), and its host-only calls behave (no GPU needed)."""
+import ctypes as C
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_c_functions():
+    names = set()
+    for h in ("prefree_b200.h",):
+        text = open(os.path.join(ROOT, "include", h)).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        for m in re.finditer(r"\b(?:pf_status|void|const char \*|uint64_t)\s+(pf_\w+)\s*\(", text):
+            names.add(m.group(1))
+    return sorted(names)
+
+
+def test_every_declared_symbol_is_exported(pf):
+    out = subprocess.run(["nm", "-D", "--defined-only", pf.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {l.split()[-1] for l in out.splitlines() if l.strip()}
+    decl = declared_c_functions()
+    assert len(decl) >= 25
+    missing = [s for s in decl if s not in exported]
+    assert not missing, missing
+    for s in pf.CXX_EXPORTED:
+        assert s in exported, s
+    assert set(decl) <= set(pf.EXPORTED) | {"pf_spmv_noalloc_f64_i32"}
+
+
+def test_cxx_symbol_demangles_to_reference_signature(pf):
+    out = subprocess.run(["c++filt", "_Z11preFreeSpMVPdPiS0_S_S_iiiS_S_"], capture_output=True,
+                         text=True).stdout.strip()
+    assert out == "preFreeSpMV(double*, int*, int*, double*, double*, int, int, int, double*, double*)"
+
+
+def test_version_and_errors(pf):
+    assert "sm_100a" in pf.version()
+    with pytest.raises(pf.PfError) as e:
+        pf.mmio_read("/nonexistent/file.mtx")
+    assert e.value.status == 5
+    assert b"cannot open" in pf.lib.pf_last_error()
+
+
+def test_handle_without_gpu_reports_error(pf):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    h = C.c_void_p()
+    st = pf.lib.pf_handle_create(C.byref(h))
+    assert st == 2                        # PF_ERR_CUDA, no crash
+    assert pf.lib.pf_last_error()
+
+
+def test_null_and_bad_arguments(pf):
+    # argument checks run before any CUDA call
+    st = pf.lib.pf_spmv_f64_i32(None, 1, 1, 0, None, None, None, 1.0, None, 0.0, None, None)
+    assert st == 1
+    b = np.zeros(3, dtype=np.int64)
+    assert pf.lib.pf_shard_bounds_i64(None, 2, 2, b.ctypes.data) == 1
+    s = pf.pf_gen_spec(9, 0, 1, 0, 0, 0)
+    assert pf.lib.pf_gen_resolve(C.byref(s)) == 1
+
+
+def test_shard_bounds(pf):
+    rp = np.array([0, 5, 5, 9, 20, 21, 30], dtype=np.int64)
+    b = pf.shard_bounds(rp, 3)
+    assert b[0] == 0 and b[-1] == 6 and np.all(np.diff(b) >= 0)
+    # bounds[k] = first row starting at or after k*nnz/parts
+    for k in range(1, 3):
+        assert rp[b[k]] >= 30 * k // 3 and (b[k] == 0 or rp[b[k] - 1] < 30 * k // 3)
+    assert np.array_equal(pf.shard_bounds(rp.astype(np.int32), 3), b)
