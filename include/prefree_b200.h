@@ -94,6 +94,26 @@ pf_status pf_spmv_f32_i64(pf_handle h, int64_t m, int64_t n, int64_t nnz,
                           const float *val, double alpha, const float *x,
                           double beta, float *y, void *stream);
 
+/* ---- allocation-free multiply (fp64 values, int32 row_ptr) ------------------
+ * No counterpart in the reference. For callers that cannot allocate device
+ * memory: code running inside an application that has already reserved the
+ * GPU's memory for itself, or that must not call cudaMalloc/cudaFree mid-run
+ * (they can synchronize the device and fail under memory pressure). Same
+ * arguments and result as pf_spmv_f64_i32 without a handle; always uses the
+ * NNZSPLIT kernel, whose scratch (cut-row partials, slice counters, error
+ * word) is a ~41 KB array built into the library and held by every GPU that
+ * loads it until the process exits. At most 2048 CTA slices (the SM count
+ * times the kernel's occupancy: 444 on a B200); more are refused with
+ * PF_ERR_UNSUPPORTED. The first call on a device sets it up (looks up the
+ * array's device address, sets the kernel's shared-memory limit): make it
+ * before any stream capture. Calls share the array, so calls that overlap on
+ * the GPU race. Returns after the multiply has finished on `stream`, with
+ * PF_ERR_DEVICE if the kernel flagged an error.                              */
+pf_status pf_spmv_noalloc_f64_i32(int64_t m, int64_t n, int64_t nnz,
+                                  const int32_t *row_ptr, const int32_t *col_idx,
+                                  const double *val, double alpha, const double *x,
+                                  double beta, double *y, void *stream);
+
 /* ---- host-buffer call (one multiply, copies in and out) ---------------------
  * Same arithmetic as pf_spmv_*, on HOST arrays: copies row_ptr/col/val/x in
  * (and y when beta != 0), multiplies once, copies y out, synchronizes. Device

@@ -39,6 +39,7 @@ EXPORTED = [
     "pf_mmio_read", "pf_free", "pf_shard_bounds_i32", "pf_shard_bounds_i64",
     "pf_gen_resolve", "pf_gen_count", "pf_gen_row_lengths_host", "pf_gen_rows_host",
     "pf_gen_x_host", "pf_gen_rows_device", "pf_gen_x_device",
+    "pf_spmv_noalloc_f64_i32",
 ]
 # the C++ drop-in symbols of include/PreFree.h (mangled)
 CXX_EXPORTED = [
@@ -81,6 +82,8 @@ def _load():
         f = getattr(lib, name)
         f.argtypes = [vp, i64, i64, i64, vp, vp, vp, dbl, vp, dbl, vp, vp]
         f.restype = st
+    lib.pf_spmv_noalloc_f64_i32.argtypes = [i64, i64, i64, vp, vp, vp, dbl, vp, dbl, vp, vp]
+    lib.pf_spmv_noalloc_f64_i32.restype = st
     lib.pf_prefree_spmv_f64_i32.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32,
                                             C.POINTER(dbl), C.POINTER(dbl)]
     lib.pf_prefree_spmv_f32_i32.argtypes = lib.pf_prefree_spmv_f64_i32.argtypes

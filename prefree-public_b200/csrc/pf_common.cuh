@@ -40,6 +40,7 @@ enum : unsigned {
 
 // Count of our kernels launched since library load (bench reports it).
 extern unsigned long long g_launch_count;
+void count_launches(unsigned long long k);
 
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) {
   return (a + b - 1) / b;

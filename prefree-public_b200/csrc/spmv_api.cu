@@ -33,6 +33,8 @@ static void count_launch(unsigned long long k = 1) {
   g_launch_count += k;
 }
 
+void count_launches(unsigned long long k) { count_launch(k); }
+
 }  // namespace pf
 
 // Per-device state: scratch for cut-row carries, error word, cached buffers

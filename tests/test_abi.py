@@ -31,7 +31,7 @@ def test_every_declared_symbol_is_exported(pf):
     assert not missing, missing
     for s in pf.CXX_EXPORTED:
         assert s in exported, s
-    assert set(decl) <= set(pf.EXPORTED) | {"pf_spmv_noalloc_f64_i32"}
+    assert set(decl) <= set(pf.EXPORTED)
 
 
 def test_cxx_symbol_demangles_to_reference_signature(pf):
