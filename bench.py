@@ -180,6 +180,50 @@ def run_reference(args, rank):
     }), flush=True)
 
 
+def run_kernel_mode(args):
+    """--mode kernel: one config, one GPU, back-to-back multiplies of the
+    device-resident matrix (L2 warm between launches, as in the reference's
+    4000-launch loop, preFreeSpMV.cu:632-642). Prints one JSON line per
+    config with the per-launch time, algorithmic GB/s and the fraction of the
+    measured copy bandwidth. Used for the per-config table and ncu captures."""
+    import torch
+    pf = importlib.import_module("prefree-public_b200")
+    hbm_peak, peak_src = peaks()
+    h = pf.Handle()
+    h.set_variant(args.variant)
+    for cfg in [int(c) for c in args.config.split(",")]:
+        for vname in args.dtype.split(","):
+            vdt = torch.float64 if vname == "f64" else torch.float32
+            spec = pf.GenSpec(cfg=cfg, seed=SEED, m=args.rows, n=args.cols).resolved()
+            idt = torch.int64 if (cfg == 5 or args.int64) else torch.int32
+            rp, col, val = pf.gen_rows_device(spec, index_dtype=idt, value_dtype=vdt)
+            x = pf.gen_x_device(spec, value_dtype=vdt)
+            y = torch.empty(spec.m, dtype=vdt, device="cuda")
+            z = col.numel()
+            for _ in range(args.warmup):
+                pf.spmv(h, spec.m, spec.n, z, rp, col, val, x, y)
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                pf.spmv(h, spec.m, spec.n, z, rp, col, val, x, y)
+            e1.record()
+            torch.cuda.synchronize()
+            assert h.device_error() == 0
+            ms = e0.elapsed_time(e1) / args.steps
+            B = pf.compulsory_bytes(spec.m, spec.n, z, val.element_size(), rp.element_size())
+            print(json.dumps({"mode": "kernel", "config": cfg, "dtype": vname, "m": spec.m,
+                              "n": spec.n, "nnz": z, "variant": args.variant, "us": ms * 1e3,
+                              "gflops": 2 * z / ms / 1e6, "alg_GBps": B / ms / 1e6,
+                              "frac_of_" + peak_src: B / ms / 1e6 / hbm_peak,
+                              "frac_of_8TBps": B / ms / 1e6 / 8000.0,
+                              "launches": args.steps}), flush=True)
+            del rp, col, val, x, y
+            torch.cuda.empty_cache()
+    h.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -189,7 +233,19 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--mode", default="power", choices=["power", "kernel"],
+                    help="power: the config-5 power iteration (the benchmark line); "
+                         "kernel: per-config single-GPU multiply timing")
+    ap.add_argument("--config", default="1,2,3,4,5", help="kernel mode: configs")
+    ap.add_argument("--dtype", default="f64", help="kernel mode: f64 and/or f32")
+    ap.add_argument("--variant", type=int, default=0, help="kernel mode: 0 auto, 1-4 forced")
+    ap.add_argument("--rows", type=int, default=0, help="kernel mode: override m")
+    ap.add_argument("--cols", type=int, default=0, help="kernel mode: override n")
+    ap.add_argument("--int64", action="store_true", help="kernel mode: int64 row_ptr")
     args = ap.parse_args()
+    if args.mode == "kernel":
+        run_kernel_mode(args)
+        return
     assert args.warmup >= 3 or args.impl == "reference" or os.environ.get("PF_BENCH_ALLOW_SHORT"), \
         "at least 3 warm-up steps"
 

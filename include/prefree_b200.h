@@ -46,7 +46,10 @@ typedef enum pf_variant {
   PF_VARIANT_NNZSPLIT = 1, /* nnz-balanced CTA slices, any row length        */
   PF_VARIANT_ROWGROUP = 2, /* row-aligned slices, warp lanes per row (short) */
   PF_VARIANT_NNZSPLIT_LDG = 3, /* NNZSPLIT with plain coalesced loads (no TMA) */
-  PF_VARIANT_ROWVEC = 4    /* row-aligned, 16-byte block loads per lane        */
+  PF_VARIANT_ROWVEC = 4,   /* row-aligned, 16-byte block loads per lane        */
+  PF_VARIANT_ROWVEC_LX = 5, /* ROWVEC + long rows finished in balanced chunks  */
+  PF_VARIANT_ROWSTREAM = 6, /* row tiles staged in shared memory by bulk copies */
+  PF_VARIANT_ROWSTREAM_LX = 7 /* ROWSTREAM + long-row chunks for unstaged tiles */
 } pf_variant;
 
 typedef struct pf_handle_s *pf_handle;

@@ -11,6 +11,7 @@
 #include "spmv_nnzsplit.cuh"
 #include "spmv_rowgroup.cuh"
 #include "spmv_rowvec.cuh"
+#include "spmv_rowstream.cuh"
 #include "spmv_tma.cuh"
 
 namespace pf {
@@ -68,6 +69,11 @@ struct pf_handle_s {
   int64_t cap = 0;
   bool scratch_dirty = false;
   unsigned *err = nullptr;
+  // long-row escape list (ROWVEC_LX), one allocation, zeroed when grown
+  void *lx_buf = nullptr;
+  size_t lx_bytes = 0;
+  bool lx_dirty = false;
+  pf::LongRowScratch lx{};
   // host-call buffers
   void *hbuf[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
   size_t hcap[5] = {0, 0, 0, 0, 0};
@@ -92,6 +98,45 @@ static pf_status ensure_scratch(pf_handle h, int64_t num_ctas, cudaStream_t st) 
     PF_CUDA_TRY(cudaMemsetAsync(h->counters, 0, sizeof(unsigned) * h->cap, st));
     h->scratch_dirty = false;
   }
+  return PF_OK;
+}
+
+constexpr int64_t kLxChunk = 1024;  // non-zeros per long-row chunk
+
+static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+// Long-row list sized for the worst case of this nnz: at most nnz/(lt+1)
+// rows can be longer than lt, and they hold at most nnz/chunk + entries chunks.
+static pf_status ensure_lx(pf_handle h, int64_t nnz, int64_t lt, cudaStream_t st) {
+  const int64_t ce = nnz / (lt + 1) + 1;
+  const int64_t cc = ceil_div(nnz, kLxChunk) + ce;
+  if (ce <= h->lx.cap_entries && cc <= h->lx.cap_chunks && !h->lx_dirty) return PF_OK;
+  const int64_t cap_e = std::max(ce, h->lx.cap_entries), cap_c = std::max(cc, h->lx.cap_chunks);
+  const size_t b_hdr = 256;
+  const size_t b_ent = align256(sizeof(LongRowEntry) * (size_t)cap_e);
+  const size_t b_cnt = align256(sizeof(unsigned) * (size_t)cap_e);
+  const size_t b_part = align256(sizeof(double) * (size_t)cap_c);
+  const size_t total = b_hdr + b_ent + b_cnt + b_part;
+  if (total > h->lx_bytes) {
+    if (h->lx_buf) cudaFree(h->lx_buf);
+    h->lx_buf = nullptr;
+    h->lx_bytes = 0;
+    PF_CUDA_TRY(cudaMalloc(&h->lx_buf, total));
+    h->lx_bytes = total;
+  }
+  char *b = (char *)h->lx_buf;
+  h->lx.alloc = (unsigned long long *)b;
+  h->lx.next = (unsigned *)(b + 8);
+  h->lx.done = (unsigned *)(b + 12);
+  h->lx.ent = (LongRowEntry *)(b + b_hdr);
+  h->lx.ent_cnt = (unsigned *)(b + b_hdr + b_ent);
+  h->lx.part = (double *)(b + b_hdr + b_ent + b_cnt);
+  h->lx.cap_entries = cap_e;
+  h->lx.cap_chunks = cap_c;
+  // counters start at zero (afterwards the kernels leave them at zero)
+  PF_CUDA_TRY(cudaMemsetAsync(h->lx_buf, 0, b_hdr, st));
+  PF_CUDA_TRY(cudaMemsetAsync(h->lx.ent_cnt, 0, b_cnt, st));
+  h->lx_dirty = false;
   return PF_OK;
 }
 
@@ -138,6 +183,13 @@ static int rowgroup_lanes(double avg) {
   return v;
 }
 
+// ROWSTREAM lanes: one to two 8-element steps per lane for an average row
+static int rowstream_lanes(double avg) {
+  int v = 1;
+  while (v < 32 && 6 * v < avg) v *= 2;
+  return v;
+}
+
 // ROWVEC lanes: one 4-element block per lane covers an average row
 static int rowvec_lanes(double avg) {
   int v = 2;
@@ -164,8 +216,8 @@ static pf_variant_choice choose_from_stats(int64_t m, int64_t nnz, int64_t sampl
     ch.variant = PF_VARIANT_ROWVEC;
     ch.lanes = rowvec_lanes(avg);
   } else {
-    ch.variant = PF_VARIANT_NNZSPLIT;
-    ch.lanes = 32;
+    ch.variant = PF_VARIANT_ROWVEC_LX;
+    ch.lanes = rowvec_lanes(avg);
   }
   return ch;
 }
@@ -175,8 +227,10 @@ static pf_status select_variant(pf_handle h, int64_t m, int64_t nnz, const IT *r
                                 cudaStream_t st, pf_variant_choice *out) {
   if (h->variant != PF_VARIANT_AUTO) {
     const double avg = m > 0 ? (double)nnz / (double)m : 0.0;
-    *out = pf_variant_choice{h->variant, h->variant == PF_VARIANT_ROWVEC ? rowvec_lanes(avg)
-                                                                         : rowgroup_lanes(avg)};
+    const bool rv = h->variant == PF_VARIANT_ROWVEC || h->variant == PF_VARIANT_ROWVEC_LX;
+    const bool rs = h->variant == PF_VARIANT_ROWSTREAM || h->variant == PF_VARIANT_ROWSTREAM_LX;
+    *out = pf_variant_choice{h->variant, rs ? rowstream_lanes(avg)
+                                            : rv ? rowvec_lanes(avg) : rowgroup_lanes(avg)};
     return PF_OK;
   }
   for (int i = 0; i < h->cache_n; ++i) {
@@ -221,14 +275,66 @@ static pf_status launch_rowgroup(pf_handle h, const SpmvParams<VT, IT> &prm, cud
 }
 
 template <typename VT, typename IT, int V>
-static pf_status launch_rowvec(pf_handle h, const SpmvParams<VT, IT> &prm, cudaStream_t st) {
+static pf_status launch_rowvec(pf_handle h, const SpmvParams<VT, IT> &prm, bool lx,
+                               cudaStream_t st) {
   constexpr int U = 2, NTB = 256;
   const int64_t rows_per_block = (int64_t)(NTB / 32) * (32 / V) * U;
   const int64_t want = ceil_div(prm.m, rows_per_block);
   const int64_t cap = (int64_t)h->num_sms * 16;
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min(want, cap));
-  spmv_rowvec_kernel<VT, IT, V, U, NTB><<<grid, NTB, 0, st>>>(prm);
+  if (!lx) {
+    spmv_rowvec_kernel<VT, IT, V, U, NTB, false>
+        <<<grid, NTB, 0, st>>>(prm, LongRowScratch{}, INT64_MAX, kLxChunk);
+    count_launch();
+    PF_CUDA_TRY(cudaGetLastError());
+    return PF_OK;
+  }
+  // rows longer than four block-steps of the group go to the chunk kernel
+  const int64_t lt = 16 * V;
+  pf_status s = ensure_lx(h, prm.nnz, lt, st);
+  if (s != PF_OK) return s;
+  spmv_rowvec_kernel<VT, IT, V, U, NTB, true><<<grid, NTB, 0, st>>>(prm, h->lx, lt, kLxChunk);
+  spmv_longrow_chunks_kernel<VT, IT, 256>
+      <<<(unsigned)(h->num_sms * 4), 256, 0, st>>>(prm, h->lx, kLxChunk);
+  count_launch(2);
+  PF_CUDA_TRY(cudaGetLastError());
+  return PF_OK;
+}
+
+template <typename VT, typename IT, int V>
+static pf_status launch_rowstream(pf_handle h, const SpmvParams<VT, IT> &prm, bool lx,
+                                  cudaStream_t st) {
+  using C = RowStreamCfg;
+  static int occ[2] = {-1, -1};
+  const size_t smem = sizeof(RowStreamSmem<VT, IT>);
+  auto kern = lx ? spmv_rowstream_kernel<VT, IT, V, true> : spmv_rowstream_kernel<VT, IT, V, false>;
+  int &o = occ[lx ? 1 : 0];
+  if (o < 0) {
+    PF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int v = 0;
+    PF_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kern, C::NTP, smem));
+    o = std::max(1, v);
+  }
+  constexpr int GROUPS = C::NT / V;
+  const double avg = (double)prm.nnz / (double)prm.m;
+  int rpg = (int)(0.75 * C::CAP / (std::max(avg, 1.0) * GROUPS));
+  rpg = std::max(1, std::min(rpg, C::RMAX / GROUPS));
+  const int64_t R = (int64_t)GROUPS * rpg;
+  const int64_t ntiles = ceil_div(prm.m, R);
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(ntiles, (int64_t)h->num_sms * o));
+  const int lt = 16 * V;                 // longer in-tile rows: one warp each
+  const int64_t lx_lt = 256;             // longer rows of unstaged tiles: chunk kernel
+  if (lx) {
+    pf_status s = ensure_lx(h, prm.nnz, lx_lt, st);
+    if (s != PF_OK) return s;
+  }
+  kern<<<grid, C::NTP, smem, st>>>(prm, lx ? h->lx : LongRowScratch{}, rpg, lt, lx_lt, kLxChunk);
   count_launch();
+  if (lx) {
+    spmv_longrow_chunks_kernel<VT, IT, 256>
+        <<<(unsigned)(h->num_sms * 4), 256, 0, st>>>(prm, h->lx, kLxChunk);
+    count_launch();
+  }
   PF_CUDA_TRY(cudaGetLastError());
   return PF_OK;
 }
@@ -284,22 +390,44 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
   prm.err = h->err;
 
   // ROWVEC needs 16-byte aligned col/val (16-byte block loads)
+  if (ch.variant == PF_VARIANT_ROWVEC_LX && (((uintptr_t)col | (uintptr_t)val) & 15) != 0) {
+    ch.variant = PF_VARIANT_NNZSPLIT;  // irregular rows, unaligned arrays
+  }
   if (ch.variant == PF_VARIANT_ROWVEC &&
       (((uintptr_t)col | (uintptr_t)val) & 15) != 0) {
     ch.variant = PF_VARIANT_ROWGROUP;
     ch.lanes = rowgroup_lanes(m > 0 ? (double)nnz / (double)m : 0.0);
   }
-  if (ch.variant == PF_VARIANT_ROWVEC) {
+  if (ch.variant == PF_VARIANT_ROWSTREAM || ch.variant == PF_VARIANT_ROWSTREAM_LX) {
+    // the long-row chunk kernel uses 16-byte loads: unaligned col/val keep
+    // long rows of unstaged tiles in the row kernel instead
+    const bool lx = ch.variant == PF_VARIANT_ROWSTREAM_LX &&
+                    (((uintptr_t)col | (uintptr_t)val) & 15) == 0;
     prm.T = 0;
     prm.num_ctas = 0;
     prm.carry_head = prm.carry_tail = nullptr;
     prm.counters = nullptr;
     switch (ch.lanes) {
-      case 2: return launch_rowvec<VT, IT, 2>(h, prm, st);
-      case 4: return launch_rowvec<VT, IT, 4>(h, prm, st);
-      case 8: return launch_rowvec<VT, IT, 8>(h, prm, st);
-      case 16: return launch_rowvec<VT, IT, 16>(h, prm, st);
-      default: return launch_rowvec<VT, IT, 32>(h, prm, st);
+      case 1: return launch_rowstream<VT, IT, 1>(h, prm, lx, st);
+      case 2: return launch_rowstream<VT, IT, 2>(h, prm, lx, st);
+      case 4: return launch_rowstream<VT, IT, 4>(h, prm, lx, st);
+      case 8: return launch_rowstream<VT, IT, 8>(h, prm, lx, st);
+      case 16: return launch_rowstream<VT, IT, 16>(h, prm, lx, st);
+      default: return launch_rowstream<VT, IT, 32>(h, prm, lx, st);
+    }
+  }
+  if (ch.variant == PF_VARIANT_ROWVEC || ch.variant == PF_VARIANT_ROWVEC_LX) {
+    const bool lx = ch.variant == PF_VARIANT_ROWVEC_LX;
+    prm.T = 0;
+    prm.num_ctas = 0;
+    prm.carry_head = prm.carry_tail = nullptr;
+    prm.counters = nullptr;
+    switch (ch.lanes) {
+      case 2: return launch_rowvec<VT, IT, 2>(h, prm, lx, st);
+      case 4: return launch_rowvec<VT, IT, 4>(h, prm, lx, st);
+      case 8: return launch_rowvec<VT, IT, 8>(h, prm, lx, st);
+      case 16: return launch_rowvec<VT, IT, 16>(h, prm, lx, st);
+      default: return launch_rowvec<VT, IT, 32>(h, prm, lx, st);
     }
   }
   if (ch.variant == PF_VARIANT_ROWGROUP) {
@@ -442,6 +570,7 @@ pf_status pf_handle_destroy(pf_handle h) {
   if (h->err) cudaFree(h->err);
   for (int i = 0; i < 5; ++i)
     if (h->hbuf[i]) cudaFree(h->hbuf[i]);
+  if (h->lx_buf) cudaFree(h->lx_buf);
   if (h->sample_dev) cudaFree(h->sample_dev);
   if (h->sample_host) cudaFreeHost(h->sample_host);
   cudaSetDevice(cur);
@@ -451,7 +580,7 @@ pf_status pf_handle_destroy(pf_handle h) {
 
 pf_status pf_handle_set_variant(pf_handle h, int variant) {
   PF_CHECK_ARG(h != nullptr, "null handle");
-  PF_CHECK_ARG(variant >= PF_VARIANT_AUTO && variant <= PF_VARIANT_ROWVEC,
+  PF_CHECK_ARG(variant >= PF_VARIANT_AUTO && variant <= PF_VARIANT_ROWSTREAM_LX,
                "unknown variant %d", variant);
   h->variant = variant;
   return PF_OK;
@@ -473,6 +602,7 @@ pf_status pf_handle_device_error(pf_handle h, uint32_t *bits, int clear) {
   if (clear && v) {
     PF_CUDA_TRY(cudaMemset(h->err, 0, sizeof(unsigned)));
     h->scratch_dirty = true;  // a failed launch may leave counters set
+    h->lx_dirty = true;
   }
   return PF_OK;
 }

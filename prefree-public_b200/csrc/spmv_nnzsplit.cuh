@@ -50,6 +50,23 @@ struct SpmvParams {
   unsigned *err;        // device error word
 };
 
+// Long-row escape list (ROWVEC_LX): rows longer than the short-row limit are
+// listed by the row kernel and finished by the chunk kernel. All counters are
+// zero between launches (the chunk kernel's last CTA resets them).
+struct LongRowEntry {
+  int64_t row, s, e, base;  // row, its non-zero range, first chunk id
+};
+
+struct LongRowScratch {
+  unsigned long long *alloc;  // high 32 bits: entries, low 32 bits: chunks
+  LongRowEntry *ent;          // [cap_entries], in chunk-base order
+  unsigned *ent_cnt;          // per entry: chunks finished
+  double *part;               // [cap_chunks] chunk partials
+  unsigned *next;             // next chunk to take
+  unsigned *done;             // CTAs finished
+  int64_t cap_entries, cap_chunks;
+};
+
 // Smallest idx in [0, m] with row_ptr[idx] >= key (row_ptr[m] >= key assumed).
 // One warp, 32 probes per step: ~log32(m) dependent loads.
 template <typename IT>

@@ -51,9 +51,14 @@ struct Block4<float> {
   }
 };
 
-template <typename VT, typename IT, int V, int U, int NTB>
+// LX (long-row escape): a row longer than `lt` non-zeros is not summed here;
+// lane 0 of its group lists it (one 64-bit atomic reserves a list slot and
+// its chunk ids in one step, so list order = chunk-base order) and
+// spmv_longrow_chunks_kernel finishes it.
+template <typename VT, typename IT, int V, int U, int NTB, bool LX>
 __global__ void __launch_bounds__(NTB)
-spmv_rowvec_kernel(const SpmvParams<VT, IT> P) {
+spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t lt,
+                   int64_t chunk) {
   constexpr int GPW = 32 / V;  // row groups per warp
   constexpr int64_t RPW = (int64_t)GPW * U;
   const int lane = threadIdx.x & 31;
@@ -83,9 +88,26 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P) {
     }
     double acc[U];
     int64_t q[U];
+    bool skip[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       acc[u] = 0.0;
+      skip[u] = false;
+      if (LX && e[u] - s[u] > lt) {
+        skip[u] = true;
+        if (lig == 0) {
+          const unsigned long long nch = (unsigned long long)((e[u] - s[u] + chunk - 1) / chunk);
+          const unsigned long long old = atomicAdd(L.alloc, (1ull << 32) | nch);
+          const int64_t idx = (int64_t)(old >> 32);
+          const int64_t base = (int64_t)(old & 0xffffffffull);
+          if (idx < L.cap_entries && base + (int64_t)nch <= L.cap_chunks) {
+            L.ent[idx] = LongRowEntry{rb + (int64_t)u * GPW + gw, s[u], e[u], base};
+          } else {
+            atomicOr(P.err, PF_DEVERR_ROWPTR);
+          }
+        }
+        e[u] = s[u];  // nothing to sum here
+      }
       q[u] = (s[u] & ~(int64_t)3) + 4 * lig;
     }
     bool bad = false;
@@ -131,7 +153,7 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P) {
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int64_t r = rb + (int64_t)u * GPW + gw;
-        if (r < P.m) {
+        if (r < P.m && !skip[u]) {
           double out = alpha * acc[u];
           if (beta != 0.0) out += beta * (double)P.y[r];
           P.y[r] = (VT)out;
@@ -142,6 +164,84 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P) {
     for (int u = 0; u < U; ++u) {
       s[u] = ns[u];
       e[u] = ne[u];
+    }
+  }
+}
+
+// Chunks of the listed long rows: warps take 1024-non-zero chunks
+// dynamically, sum them with 16-byte block loads, store the partial; the last
+// chunk of a row to finish sums the row's partials in chunk order (the same
+// order on every run) and writes y. The last CTA resets the counters.
+template <typename VT, typename IT, int NTB>
+__global__ void __launch_bounds__(NTB)
+spmv_longrow_chunks_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t chunk) {
+  const int lane = threadIdx.x & 31;
+  const unsigned long long a = *((volatile unsigned long long *)L.alloc);
+  const int64_t n_ent = (int64_t)(a >> 32);
+  const int64_t n_chunks = (int64_t)(a & 0xffffffffull);
+  const uint32_t n = (uint32_t)(P.n < 0xffffffffLL ? P.n : 0xffffffffLL);
+  bool bad = false;
+  while (n_chunks > 0) {
+    int64_t g = 0;
+    if (lane == 0) g = (int64_t)atomicAdd(L.next, 1u);
+    g = __shfl_sync(0xffffffffu, g, 0);
+    if (g >= n_chunks) break;
+    // entry with the largest base <= g
+    int64_t lo = 0, hi = n_ent - 1;
+    while (lo < hi) {
+      const int64_t mid = (lo + hi + 1) >> 1;
+      if (__ldcg(&L.ent[mid].base) <= g) lo = mid;
+      else hi = mid - 1;
+    }
+    const LongRowEntry E = L.ent[lo];
+    const int64_t k = g - E.base;
+    const int64_t cs = E.s + k * chunk;
+    const int64_t ce = min(cs + chunk, E.e);
+    double acc = 0.0;
+    for (int64_t q = (cs & ~(int64_t)3) + 4 * lane; q < ce; q += 4 * 32) {
+      const int4 c4 = __ldcs(reinterpret_cast<const int4 *>(P.col + q));
+      VT v4[4];
+      Block4<VT>::load(P.val, q, q + 1 >= cs, q + 2 < ce, v4);
+      const int cc[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t el = q + i;
+        const bool use = el >= cs && el < ce;
+        const bool inb = (uint32_t)cc[i] < n;
+        bad |= use && !inb;
+        const VT xv = (use && inb) ? __ldg(P.x + cc[i]) : VT(0);
+        acc += (double)v4[i] * (double)xv;
+      }
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d);
+    if (lane == 0) {
+      L.part[g] = acc;
+      __threadfence();
+      const unsigned nch = (unsigned)((E.e - E.s + chunk - 1) / chunk);
+      const unsigned old = atomicAdd(&L.ent_cnt[lo], 1u);
+      if (old == nch - 1) {
+        __threadfence();
+        double sum = 0.0;
+        for (unsigned c = 0; c < nch; ++c) sum += __ldcg(&L.part[E.base + c]);
+        double out = P.alpha * sum;
+        if (P.beta != 0.0) out += P.beta * (double)P.y[E.row];
+        P.y[E.row] = (VT)out;
+        L.ent_cnt[lo] = 0;
+      }
+    }
+  }
+  if (bad) atomicOr(P.err, PF_DEVERR_BOUNDS);
+  // last CTA out resets the work counters for the next launch
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned old = atomicAdd(L.done, 1u);
+    if (old == gridDim.x - 1) {
+      *L.next = 0;
+      *L.alloc = 0ull;
+      *L.done = 0;
+      __threadfence();
     }
   }
 }

@@ -71,7 +71,8 @@ def check(oracle, y, rp, col, val, x, vdt, alpha=1.0, beta=0.0, y0=None):
     assert ok, f"{nbad} rows out of tolerance (worst ratio {worst:.3g})"
 
 
-VARIANTS = {"auto": 0, "nnzsplit": 1, "rowgroup": 2, "nnzsplit_ldg": 3, "rowvec": 4}
+VARIANTS = {"auto": 0, "nnzsplit": 1, "rowgroup": 2, "nnzsplit_ldg": 3, "rowvec": 4,
+            "rowvec_lx": 5, "rowstream": 6, "rowstream_lx": 7}
 
 
 @pytest.fixture
@@ -105,7 +106,8 @@ def test_small_slices_force_cut_rows(pf, oracle, torch_cuda, variant_handle, nam
     check(oracle, y, rp, col, val, x, np.float64)
 
 
-@pytest.mark.parametrize("variant_handle", ["nnzsplit", "rowgroup", "rowvec"], indirect=True)
+@pytest.mark.parametrize("variant_handle", ["nnzsplit", "rowgroup", "rowvec", "rowvec_lx",
+                                            "rowstream", "rowstream_lx"], indirect=True)
 @pytest.mark.parametrize("offset", [1, 2, 3, 5])
 def test_unaligned_array_starts(pf, oracle, torch_cuda, variant_handle, offset):
     """val/col/row_ptr that do not start on a 16-byte boundary (views into
