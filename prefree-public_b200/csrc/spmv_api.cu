@@ -190,10 +190,12 @@ static int rowstream_lanes(double avg) {
   return v;
 }
 
-// ROWVEC lanes: one 4-element block per lane covers an average row
+// ROWVEC lanes: one 4-element block per lane covers an average row; long
+// rows use 16 lanes (measured faster than 32 on 2000-non-zero rows: more
+// rows in flight per warp)
 static int rowvec_lanes(double avg) {
   int v = 2;
-  while (v < 32 && 4 * v < avg) v *= 2;
+  while (v < 16 && 4 * v < avg) v *= 2;
   return v;
 }
 
@@ -277,13 +279,16 @@ static pf_status launch_rowgroup(pf_handle h, const SpmvParams<VT, IT> &prm, cud
 template <typename VT, typename IT, int V>
 static pf_status launch_rowvec(pf_handle h, const SpmvParams<VT, IT> &prm, bool lx,
                                cudaStream_t st) {
-  constexpr int U = 2, NTB = 256;
+  // U = 2 rows per lane group in flight, built for 4 CTAs per SM (64
+  // registers): the best of a sweep over V, U and the CTA bound on configs
+  // 1, 2, 4 and 5
+  constexpr int U = 2, NTB = 256, MINB = 4;
   const int64_t rows_per_block = (int64_t)(NTB / 32) * (32 / V) * U;
   const int64_t want = ceil_div(prm.m, rows_per_block);
   const int64_t cap = (int64_t)h->num_sms * 16;
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min(want, cap));
   if (!lx) {
-    spmv_rowvec_kernel<VT, IT, V, U, NTB, false>
+    spmv_rowvec_kernel<VT, IT, V, U, NTB, false, MINB>
         <<<grid, NTB, 0, st>>>(prm, LongRowScratch{}, INT64_MAX, kLxChunk);
     count_launch();
     PF_CUDA_TRY(cudaGetLastError());
@@ -293,7 +298,7 @@ static pf_status launch_rowvec(pf_handle h, const SpmvParams<VT, IT> &prm, bool 
   const int64_t lt = 16 * V;
   pf_status s = ensure_lx(h, prm.nnz, lt, st);
   if (s != PF_OK) return s;
-  spmv_rowvec_kernel<VT, IT, V, U, NTB, true><<<grid, NTB, 0, st>>>(prm, h->lx, lt, kLxChunk);
+  spmv_rowvec_kernel<VT, IT, V, U, NTB, true, MINB><<<grid, NTB, 0, st>>>(prm, h->lx, lt, kLxChunk);
   spmv_longrow_chunks_kernel<VT, IT, 256>
       <<<(unsigned)(h->num_sms * 4), 256, 0, st>>>(prm, h->lx, kLxChunk);
   count_launch(2);

@@ -1,24 +1,33 @@
 // ROWSTREAM variant: row tiles streamed into shared memory by a producer
-// warp, summed by lane groups from shared memory.
+// warp; x gathered into shared memory with asynchronous copies one tile
+// ahead of the row sums.
 //
 // A tile is R consecutive rows (R = (NT/V) * rows_per_group, chosen so that
 // an average tile holds ~3/4 of CAP non-zeros). The producer warp's lane 0
 // streams the tile's contiguous ranges — row_ptr[r0..r0+R], val and col over
 // [row_ptr[r0], row_ptr[r0+R]) — with bulk copies (cp.async.bulk, no tensor
-// map, no multicast) into one of two stages, completing on the stage's
-// "full" mbarrier. Consumers: groups of V lanes per row; a group reads its
-// rows' col/val from shared memory (lanes on consecutive elements: no bank
-// conflicts), issues all of a lane's x gathers before using them, reduces
-// with __shfl_xor and stores y (consecutive groups, consecutive rows). Rows
-// with more than LT non-zeros are summed afterwards by whole warps (still
-// from shared memory). A tile with more than CAP non-zeros is not staged: its
-// short rows are read from global memory, and rows longer than `lx_lt` are
+// map, no multicast) into one of three stages, completing on the stage's
+// "full" mbarrier.
+//
+// Consumers, iteration k:
+//   A. wait for tile k's stage, then gather x[col] for all its non-zeros
+//      (striped over the threads) with 8-byte cp.async copies into a
+//      shared-memory buffer: no registers are held while a whole tile's
+//      gathers are in flight;
+//   B. wait for tile k-1's gathers, one barrier (which also carries the
+//      "every wait succeeded" vote), then groups of V lanes sum
+//      val*x over their rows of tile k-1 from shared memory and store y
+//      (consecutive groups, consecutive rows); rows with more than LT
+//      non-zeros are summed afterwards by whole warps; finally the stage is
+//      released on its "empty" mbarrier.
+// So tile k's gathers are in flight while tile k-1 is summed and tile k+1 is
+// being copied in. A tile with more than CAP non-zeros is not staged: its
+// groups read col/val/x from global memory, and rows longer than `lx_lt` are
 // listed for spmv_longrow_chunks_kernel when the long-row list is enabled.
-// Consumers release a stage by arriving on its "empty" mbarrier.
 //
 // Whole rows per tile: no carries, no atomics on y, deterministic. Every
-// mbarrier wait is bounded; on expiry the kernel sets PF_DEVERR_WAIT_TIMEOUT
-// and returns after waiting (bounded) for its own copies in flight.
+// mbarrier wait is bounded; on expiry the kernel sets PF_DEVERR_WAIT_TIMEOUT,
+// waits for its own asynchronous copies, and returns.
 #pragma once
 
 #include "pf_common.cuh"
@@ -31,16 +40,16 @@ namespace pf {
 struct RowStreamCfg {
   static constexpr int NT = 256;      // consumer threads
   static constexpr int NTP = NT + 32; // + producer warp
-  static constexpr int CAP = 4096;    // non-zeros per staged tile
+  static constexpr int CAP = 1536;    // non-zeros per staged tile
   static constexpr int RMAX = 512;    // rows per tile at most
-  static constexpr int NSTAGE = 2;
-  static constexpr int MAXLONG = 64;  // in-tile long rows per stage
+  static constexpr int NSTAGE = 3;    // bulk-copy stages (= gather buffers)
+  static constexpr int MAXLONG = 32;  // in-tile long rows listed per tile
 };
 
 // One stage. Every bulk copy into it starts 16-byte aligned, so each array
 // and the struct itself are multiples of 16 bytes, and each array has room
 // for the 16-byte rounding of its copy (up to 15 bytes before the first and
-// after the last element: 8 extra elements of 4 bytes or 4 of 8 bytes).
+// after the last element).
 template <typename VT, typename IT>
 struct alignas(128) RowStreamStage {
   VT val[RowStreamCfg::CAP + 32 / sizeof(VT)];
@@ -48,7 +57,6 @@ struct alignas(128) RowStreamStage {
   IT rp[RowStreamCfg::RMAX + 1 + 32 / sizeof(IT) + (sizeof(IT) == 4 ? 3 : 1)];
 };
 static_assert(sizeof(RowStreamStage<double, int64_t>) % 128 == 0, "stage size");
-static_assert(sizeof(((RowStreamStage<double, int64_t> *)0)->val) % 16 == 0, "val size");
 static_assert(sizeof(((RowStreamStage<float, int32_t> *)0)->val) % 16 == 0, "val size");
 static_assert(sizeof(((RowStreamStage<double, int64_t> *)0)->col) % 16 == 0, "col size");
 static_assert(sizeof(((RowStreamStage<double, int64_t> *)0)->rp) % 16 == 0, "rp size");
@@ -57,15 +65,26 @@ static_assert(sizeof(((RowStreamStage<double, int32_t> *)0)->rp) % 16 == 0, "rp 
 template <typename VT, typename IT>
 struct RowStreamSmem {
   RowStreamStage<VT, IT> st[RowStreamCfg::NSTAGE];
-  int2 lrow[RowStreamCfg::NSTAGE][RowStreamCfg::MAXLONG];  // (row in tile, 0)
+  VT sx[RowStreamCfg::NSTAGE][RowStreamCfg::CAP];  // gathered x, per stage
+  int lrow[RowStreamCfg::NSTAGE][RowStreamCfg::MAXLONG];
   uint64_t full[RowStreamCfg::NSTAGE];
   uint64_t empty[RowStreamCfg::NSTAGE];
-  int64_t a[RowStreamCfg::NSTAGE];     // first non-zero of the staged tile
+  int64_t a[RowStreamCfg::NSTAGE];     // first non-zero of the tile
   int dv[RowStreamCfg::NSTAGE], dc[RowStreamCfg::NSTAGE], dr[RowStreamCfg::NSTAGE];
   int staged[RowStreamCfg::NSTAGE];    // 1: val/col in shared memory
   int nlong[RowStreamCfg::NSTAGE];
-  int ok[RowStreamCfg::NSTAGE];  // per stage: a flag is rewritten only after its stage is released
 };
+
+template <typename VT>
+__device__ __forceinline__ void gather_async(VT *dst, const VT *src, bool valid);
+template <>
+__device__ __forceinline__ void gather_async<double>(double *dst, const double *src, bool valid) {
+  ptx::cp_async8(dst, src, valid);
+}
+template <>
+__device__ __forceinline__ void gather_async<float>(float *dst, const float *src, bool valid) {
+  ptx::cp_async4(dst, src, valid);
+}
 
 template <typename VT, typename IT, int V, bool LX>
 __global__ void __launch_bounds__(RowStreamCfg::NTP)
@@ -97,7 +116,6 @@ spmv_rowstream_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int rp
     if (tid != NT) return;
     const uint64_t pol = ptx::policy_evict_first();
     int64_t k = 0;
-    bool ok = true;
     // the tile's non-zero range is read one tile ahead, before the wait for
     // a free stage, so that load latency overlaps the consumers' work
     int64_t na = 0, nb = 0;
@@ -106,7 +124,7 @@ spmv_rowstream_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int rp
       na = (int64_t)__ldg(P.row_ptr + r0);
       nb = (int64_t)__ldg(P.row_ptr + min(r0 + R, P.m));
     }
-    for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++k) {
+    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++k) {
       const int s = (int)(k % NS);
       const int64_t a = na, b = nb;
       const int64_t tn = t + gridDim.x;
@@ -114,12 +132,10 @@ spmv_rowstream_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int rp
         na = (int64_t)__ldg(P.row_ptr + tn * R);
         nb = (int64_t)__ldg(P.row_ptr + min(tn * R + R, P.m));
       }
-      if (k >= NS) {
-        ok = ptx::mbar_wait_bounded(&S.empty[s], (uint32_t)((k / NS - 1) & 1), PF_WAIT_LIMIT_NS);
-        if (!ok) {
-          atomicOr(P.err, PF_DEVERR_WAIT_TIMEOUT);
-          break;
-        }
+      if (k >= NS &&
+          !ptx::mbar_wait_bounded(&S.empty[s], (uint32_t)((k / NS - 1) & 1), PF_WAIT_LIMIT_NS)) {
+        atomicOr(P.err, PF_DEVERR_WAIT_TIMEOUT);
+        break;
       }
       const int64_t r0 = t * R;
       const int64_t r1 = min(r0 + R, P.m);
@@ -160,22 +176,61 @@ spmv_rowstream_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int rp
   const int lig = tid % V;   // lane in group
   const double alpha = P.alpha, beta = P.beta;
   bool bad = false;
-  int64_t k = 0;
-  for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++k) {
-    const int s = (int)(k % NS);
-    if (tid == 0) {
-      const bool ok =
-          ptx::mbar_wait_bounded(&S.full[s], (uint32_t)((k / NS) & 1), PF_WAIT_LIMIT_NS);
-      if (!ok) atomicOr(P.err, PF_DEVERR_WAIT_TIMEOUT);
-      S.ok[s] = ok;
+  auto store_row = [&](int64_t r, double acc) {
+    double out = alpha * acc;
+    if (beta != 0.0) out += beta * (double)P.y[r];
+    P.y[r] = (VT)out;
+  };
+
+  for (int64_t k = 0;; ++k) {
+    const int64_t t = (int64_t)blockIdx.x + k * gridDim.x;  // tile gathered now
+    const bool have = t < ntiles;
+    const bool have_prev = k > 0 && t - (int64_t)gridDim.x < ntiles;  // tile summed now
+    if (!have && !have_prev) break;
+    bool ok = true;
+    // ---- A: tile t's stage, x gathers into shared memory ----------------------
+    if (have) {
+      const int s = (int)(k % NS);
+      ok = ptx::mbar_wait_bounded(&S.full[s], (uint32_t)((k / NS) & 1), PF_WAIT_LIMIT_NS);
+      if (ok && S.staged[s]) {
+        const RowStreamStage<VT, IT> &B = S.st[s];
+        const int64_t r0 = t * R;
+        const int nrows = (int)(P.m - r0 < (int64_t)R ? P.m - r0 : (int64_t)R);
+        const int tn = (int)((int64_t)B.rp[S.dr[s] + nrows] - S.a[s]);
+        const int dc = S.dc[s];
+        VT *sx = S.sx[s];
+        for (int i = tid; i < tn; i += NT) {
+          const int32_t c = B.col[i + dc];
+          const bool inb = (uint32_t)c < n;
+          bad |= !inb;
+          gather_async<VT>(sx + i, P.x + (inb ? c : 0), inb);
+        }
+      }
     }
-    ptx::named_bar_sync(1, NT);
-    if (!S.ok[s]) break;
-    const RowStreamStage<VT, IT> &B = S.st[s];
-    const bool staged = S.staged[s] != 0;
-    const int64_t a = S.a[s];
-    const int dv = S.dv[s], dc = S.dc[s], dr = S.dr[s];
-    const int64_t r0 = t * R;
+    ptx::cp_async_commit();
+    if (!have_prev) {
+      if (!ptx::named_bar_and(1, NT, ok)) {
+        if (tid == 0 && ok) atomicOr(P.err, PF_DEVERR_WAIT_TIMEOUT);
+        ptx::cp_async_wait<0>();
+        break;
+      }
+      continue;
+    }
+    // ---- B: sum tile tp = t - gridDim.x ------------------------------------------
+    ptx::cp_async_wait<1>();   // this thread's gathers for tile tp have landed
+    if (!ptx::named_bar_and(1, NT, ok)) {
+      if (tid == 0 && ok) atomicOr(P.err, PF_DEVERR_WAIT_TIMEOUT);
+      ptx::cp_async_wait<0>();
+      break;
+    }
+    const int sp = (int)((k - 1) % NS);
+    const int64_t tp = t - gridDim.x;
+    const RowStreamStage<VT, IT> &B = S.st[sp];
+    const VT *sx = S.sx[sp];
+    const bool staged = S.staged[sp] != 0;
+    const int64_t a = S.a[sp];
+    const int dv = S.dv[sp], dr = S.dr[sp];
+    const int64_t r0 = tp * R;
     const int nrows = (int)(P.m - r0 < (int64_t)R ? P.m - r0 : (int64_t)R);
 
     for (int i = 0; i < rpg; ++i) {
@@ -189,8 +244,8 @@ spmv_rowstream_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int rp
       bool store = live;
       if (live && staged && len > lt) {
         if (lig == 0) {
-          const int q = atomicAdd(&S.nlong[s], 1);
-          if (q < C::MAXLONG) S.lrow[s][q] = make_int2(j, 0);
+          const int q = atomicAdd(&S.nlong[sp], 1);
+          if (q < C::MAXLONG) S.lrow[sp][q] = j;
         }
         re = rs;
         store = false;
@@ -208,68 +263,31 @@ spmv_rowstream_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int rp
         store = false;
       }
       double acc = 0.0;
-      // 8 elements per lane per step, all gathers issued before use
-      for (int64_t e0 = rs + lig; e0 < re; e0 += 8 * V) {
-        int32_t cc[8];
-        VT vv[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int64_t el = e0 + (int64_t)u * V;
-          const bool use = el < re;
-          if (staged) {
-            const int o = (int)(el - a);
-            cc[u] = use ? B.col[o + dc] : 0;
-            vv[u] = use ? B.val[o + dv] : VT(0);
-          } else {
-            cc[u] = use ? __ldg(P.col + el) : 0;
-            vv[u] = use ? __ldcs(P.val + el) : VT(0);
-          }
+      if (staged) {
+        const int o0 = (int)(rs - a), o1 = (int)(re - a);
+        double a1 = 0.0;
+        int o = o0 + lig;
+        for (; o + V < o1; o += 2 * V) {
+          acc += (double)B.val[o + dv] * (double)sx[o];
+          a1 += (double)B.val[o + V + dv] * (double)sx[o + V];
         }
-        VT xv[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const bool use = e0 + (int64_t)u * V < re;
-          const bool inb = (uint32_t)cc[u] < n;
-          bad |= use && !inb;
-          xv[u] = (use && inb) ? __ldg(P.x + cc[u]) : VT(0);
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) acc += (double)vv[u] * (double)xv[u];
-      }
-#pragma unroll
-      for (int d = V / 2; d > 0; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d, V);
-      if (lig == 0 && store) {
-        const int64_t r = r0 + j;
-        double out = alpha * acc;
-        if (beta != 0.0) out += beta * (double)P.y[r];
-        P.y[r] = (VT)out;
-      }
-    }
-
-    // long rows of a staged tile: one warp per row, from shared memory
-    if (staged) {
-      ptx::named_bar_sync(1, NT);
-      const int nl = S.nlong[s];
-      const int nlist = nl < C::MAXLONG ? nl : C::MAXLONG;
-      for (int q = warp; q < nlist; q += NT / 32) {
-        const int j = S.lrow[s][q].x;
-        const int64_t rs = (int64_t)B.rp[dr + j], re = (int64_t)B.rp[dr + j + 1];
-        double acc = 0.0;
-        for (int64_t e0 = rs + lane; e0 < re; e0 += 8 * 32) {
+        if (o < o1) acc += (double)B.val[o + dv] * (double)sx[o];
+        acc += a1;
+      } else {
+        for (int64_t e0 = rs + lig; e0 < re; e0 += 8 * V) {
           int32_t cc[8];
           VT vv[8];
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
-            const int64_t el = e0 + (int64_t)u * 32;
+            const int64_t el = e0 + (int64_t)u * V;
             const bool use = el < re;
-            const int o = (int)(el - a);
-            cc[u] = use ? B.col[o + dc] : 0;
-            vv[u] = use ? B.val[o + dv] : VT(0);
+            cc[u] = use ? __ldg(P.col + el) : 0;
+            vv[u] = use ? __ldcs(P.val + el) : VT(0);
           }
           VT xv[8];
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
-            const bool use = e0 + (int64_t)u * 32 < re;
+            const bool use = e0 + (int64_t)u * V < re;
             const bool inb = (uint32_t)cc[u] < n;
             bad |= use && !inb;
             xv[u] = (use && inb) ? __ldg(P.x + cc[u]) : VT(0);
@@ -277,44 +295,37 @@ spmv_rowstream_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int rp
 #pragma unroll
           for (int u = 0; u < 8; ++u) acc += (double)vv[u] * (double)xv[u];
         }
+      }
+#pragma unroll
+      for (int d = V / 2; d > 0; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d, V);
+      if (lig == 0 && store) store_row(r0 + j, acc);
+    }
+
+    // long rows of a staged tile: one warp per row, from shared memory
+    if (staged) {
+      ptx::named_bar_sync(1, NT);
+      const int nl = S.nlong[sp];
+      const int nlist = nl < C::MAXLONG ? nl : C::MAXLONG;
+      auto warp_row = [&](int j) {
+        const int o0 = (int)((int64_t)B.rp[dr + j] - a), o1 = (int)((int64_t)B.rp[dr + j + 1] - a);
+        double acc = 0.0;
+        for (int o = o0 + lane; o < o1; o += 32) acc += (double)B.val[o + dv] * (double)sx[o];
 #pragma unroll
         for (int d = 16; d > 0; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d);
-        if (lane == 0) {
-          const int64_t r = r0 + j;
-          double out = alpha * acc;
-          if (beta != 0.0) out += beta * (double)P.y[r];
-          P.y[r] = (VT)out;
-        }
-      }
-      // overflow (more than MAXLONG long rows in the tile): the group pass
-      // skipped them, so sum them here by scanning the tile's rows
+        if (lane == 0) store_row(r0 + j, acc);
+      };
+      for (int q = warp; q < nlist; q += NT / 32) warp_row(S.lrow[sp][q]);
       if (nl > C::MAXLONG) {
+        // more long rows than the list holds: find the unlisted ones
         for (int j = warp; j < nrows; j += NT / 32) {
-          const int64_t rs = (int64_t)B.rp[dr + j], re = (int64_t)B.rp[dr + j + 1];
-          if (re - rs <= lt) continue;
+          if ((int64_t)B.rp[dr + j + 1] - (int64_t)B.rp[dr + j] <= lt) continue;
           bool listed = false;
-          for (int q = 0; q < C::MAXLONG; ++q) listed |= (S.lrow[s][q].x == j);
-          if (listed) continue;
-          double acc = 0.0;
-          for (int64_t el = rs + lane; el < re; el += 32) {
-            const int o = (int)(el - a);
-            const int32_t c = B.col[o + dc];
-            const bool inb = (uint32_t)c < n;
-            bad |= !inb;
-            acc += inb ? (double)B.val[o + dv] * (double)__ldg(P.x + c) : 0.0;
-          }
-#pragma unroll
-          for (int d = 16; d > 0; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d);
-          if (lane == 0) {
-            const int64_t r = r0 + j;
-            double out = alpha * acc;
-            if (beta != 0.0) out += beta * (double)P.y[r];
-            P.y[r] = (VT)out;
-          }
+          for (int q = 0; q < C::MAXLONG; ++q) listed |= (S.lrow[sp][q] == j);
+          if (!listed) warp_row(j);
         }
       }
     }
-    ptx::mbar_arrive(&S.empty[s]);
+    ptx::mbar_arrive(&S.empty[sp]);
   }
   if (bad) atomicOr(P.err, PF_DEVERR_BOUNDS);
 }

@@ -55,8 +55,8 @@ struct Block4<float> {
 // lane 0 of its group lists it (one 64-bit atomic reserves a list slot and
 // its chunk ids in one step, so list order = chunk-base order) and
 // spmv_longrow_chunks_kernel finishes it.
-template <typename VT, typename IT, int V, int U, int NTB, bool LX>
-__global__ void __launch_bounds__(NTB)
+template <typename VT, typename IT, int V, int U, int NTB, bool LX, int MINB = 1>
+__global__ void __launch_bounds__(NTB, MINB)
 spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t lt,
                    int64_t chunk) {
   constexpr int GPW = 32 / V;  // row groups per warp

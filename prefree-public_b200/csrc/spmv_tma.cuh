@@ -163,7 +163,11 @@ spmv_tma_kernel(const SpmvParams<VT, IT> P) {
       bool progressed = false;
       if (kz < nz_chunks) {
         const int slot = (int)(kz % NS);
-        if (kz < NS || ptx::mbar_test_wait(&S.empty_z[slot], (uint32_t)((kz / NS - 1) & 1))) {
+        // the val/col ring is the one that fills up: sleep on its next slot
+        // for up to ~1 us instead of spinning (the row ring is checked in
+        // between, so neither ring can starve the other)
+        if (kz < NS ||
+            ptx::mbar_try_wait_hint(&S.empty_z[slot], (uint32_t)((kz / NS - 1) & 1), 1000u)) {
           const uintptr_t sv = v_lo + (uintptr_t)kz * VCB;
           const uintptr_t sc = c_lo + (uintptr_t)kz * CCB;
           const uint32_t bv = sv < v_hi ? (uint32_t)min((uintptr_t)VCB, v_hi - sv) : 0u;
@@ -177,7 +181,10 @@ spmv_tma_kernel(const SpmvParams<VT, IT> P) {
       }
       if (kr < nr_chunks) {
         const int slot = (int)(kr % NSR);
-        if (kr < NSR || ptx::mbar_test_wait(&S.empty_r[slot], (uint32_t)((kr / NSR - 1) & 1))) {
+        const uint32_t par = (uint32_t)((kr / NSR - 1) & 1);
+        // once the val/col stream is done, sleep on the row ring instead
+        if (kr < NSR || (kz < nz_chunks ? ptx::mbar_test_wait(&S.empty_r[slot], par)
+                                        : ptx::mbar_try_wait_hint(&S.empty_r[slot], par, 1000u))) {
           const uintptr_t sr = r_lo + (uintptr_t)kr * RCB;
           const uint32_t br = (uint32_t)min((uintptr_t)RCB, r_hi - sr);
           ptx::mbar_arrive_expect_tx(&S.full_r[slot], br);
@@ -188,7 +195,7 @@ spmv_tma_kernel(const SpmvParams<VT, IT> P) {
       }
       if (progressed) {
         idle = 0;
-      } else if (__nanosleep(64), ++idle == 64) {
+      } else if (++idle == 64) {
         t_idle = ptx::globaltimer_ns();
       } else if (idle > 64 && (idle & 63) == 0 &&
                  ptx::globaltimer_ns() - t_idle > PF_WAIT_LIMIT_NS) {
