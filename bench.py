@@ -5,8 +5,10 @@ Workload (the largest config; it fits one GPU):
 64M x 64M CSR, 32 nnz/row (2^31 non-zeros), int64 row_ptr, int32 col, fp64,
 70% of columns within +-4096 of the diagonal, 30% uniform; seeded synthetic
 data (counter-based generator, seed 12345). One step = one iterated multiply
-y <- A*y/||y||: the local SpMV on each rank's equal-nnz row shard, an 8-byte
-all-reduce of ||y||^2 and an all-gather of y into every rank's x (NCCL).
+y <- A*y/||y|| over equal-nnz row shards: by default one fused kernel per rank
+(rows stored straight into every rank's next x over NVLink, ||y||^2 reduced
+in the kernel, alpha = 1/||x|| read on the device) and a cross-rank barrier;
+`--path nccl` runs the local SpMV + NCCL all-reduce/all-gather instead.
 `scaling` is "strong": the matrix is fixed, N GPUs share it.
 
 Timing: W warm-up steps, then K steps between barrier + synchronize, CUDA
@@ -233,6 +235,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--path", default="fused", choices=["fused", "nccl"],
+                    help="power mode: fused multiply + all-gather kernel, or SpMV + NCCL")
     ap.add_argument("--mode", default="power", choices=["power", "kernel"],
                     help="power: the config-5 power iteration (the benchmark line); "
                          "kernel: per-config single-GPU multiply timing")
@@ -292,7 +296,31 @@ def main():
         e1.record(stream)
         ev_pairs.append((e0, e1))
 
-    it = pfd.PowerIteration(local_spmv, x, y, bounds, rank, world)
+    if args.path == "fused":
+        # one kernel per step: rows go straight into every rank's next x over
+        # NVLink, ||y||^2 is reduced in the kernel, then a cross-rank barrier
+        fused = pfd.FusedPowerIteration(pf, h, rp, col, val, x, bounds, rank, world,
+                                        stream=stream)
+
+        class _Step:
+            def step(self):
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                pf.spmv_dist(h, m_loc, n, nnz_loc, rp, col, val, fused.xs[fused.k % 2],
+                             fused.slots[fused.k % 2], world, rank,
+                             fused.out_ptrs[(fused.k + 1) % 2].data_ptr(),
+                             fused.slot_ptrs[(fused.k + 1) % 2].data_ptr(), int(bounds[rank]),
+                             stream=stream)
+                e1.record(stream)
+                ev_pairs.append((e0, e1))
+                if fused.hdl is not None:
+                    fused.hdl.barrier(channel=0)
+                fused.k += 1
+                return None
+        it = _Step()
+    else:
+        it = pfd.PowerIteration(local_spmv, x, y, bounds, rank, world)
     for _ in range(args.warmup):
         it.step()
     torch.cuda.synchronize()
@@ -315,13 +343,17 @@ def main():
         dist.barrier()
     launches = pf.launch_count() - launches0
     step_ms = t_start.elapsed_time(t_end) / args.steps
+    if args.path == "fused":
+        final_nsq = fused.norm_sq()
+    else:
+        final_nsq = st.norm_sq
     kern_ms = sum(a.elapsed_time(b) for a, b in ev_pairs) / len(ev_pairs)
     stats = torch.tensor([step_ms, kern_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
     step_ms, kern_ms = float(stats[0]), float(stats[1])
     assert h.device_error() == 0, "device error word set"
-    final_norm = math.sqrt(st.norm_sq)
+    final_norm = math.sqrt(final_nsq)
 
     # roofline of the SpMV kernel (rank with the slowest launch)
     alg_bytes = pf.compulsory_bytes(m_loc, n, nnz_loc, 8, 8)
@@ -403,13 +435,15 @@ def main():
             "config": {"workload": WORKLOAD, "m": spec.m, "n": spec.n, "nnz": z_tot,
                        "index": "int64 row_ptr, int32 col", "parallelism": f"row shards x{world}",
                        "l2": "inputs (27 GB) larger than L2: no flush",
-                       "step": "local SpMV + all-reduce ||y||^2 + all-gather y"},
+                       "step": ("fused: SpMV storing rows into every rank's next x over NVLink + in-kernel ||y||^2 + cross-rank barrier"
+                                if args.path == "fused" else
+                                "local SpMV + NCCL all-reduce ||y||^2 + NCCL all-gather y")},
             "gpu_launches": int(launches),
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "clocks": clocks.summary(),
-            "check": {"final_norm_sq_of_y": st.norm_sq, "final_norm": final_norm},
+            "check": {"final_norm_sq_of_y": final_nsq, "final_norm": final_norm},
         }
         print(json.dumps(out), flush=True)
     h.close()

@@ -97,6 +97,31 @@ pf_status pf_spmv_f32_i64(pf_handle h, int64_t m, int64_t n, int64_t nnz,
                           const float *val, double alpha, const float *x,
                           double beta, float *y, void *stream);
 
+/* ---- fused multiply + all-gather for row-sharded iterated multiplies --------
+ * No counterpart in the reference (single GPU only). One step of
+ * x_{k+1} = A x_k / ||A x_k|| on this rank's row shard (rows
+ * [row_offset, row_offset + m) of the full matrix; row_ptr rebased to 0):
+ *   alpha = 1 / sqrt(sum of prev_slots[0..nranks));
+ *   every finished row value y_r = alpha * (A x)_r is stored straight into
+ *   out_ptrs[p][row_offset + r] for every rank p (device array of nranks
+ *   pointers: each rank's next-x buffer, peers' reachable over NVLink);
+ *   ||y||^2 of this rank's rows is reduced in the same kernel (fixed order:
+ *   the same bits every run) and stored to slot_ptrs[p][rank] for every p.
+ * The caller puts a cross-rank barrier between steps (peers' stores must
+ * land before the next step reads x, and nobody may overwrite a buffer a
+ * peer still reads: alternate two x buffers and two slot arrays). fp64 values,
+ * col/val 16-byte aligned (ROWVEC kernel). Asynchronous on `stream`.        */
+pf_status pf_spmv_dist_f64_i64(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                               const int64_t *row_ptr, const int32_t *col_idx,
+                               const double *val, const double *x, const double *prev_slots,
+                               int nranks, int rank, double *const *out_ptrs,
+                               double *const *slot_ptrs, int64_t row_offset, void *stream);
+pf_status pf_spmv_dist_f64_i32(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                               const int32_t *row_ptr, const int32_t *col_idx,
+                               const double *val, const double *x, const double *prev_slots,
+                               int nranks, int rank, double *const *out_ptrs,
+                               double *const *slot_ptrs, int64_t row_offset, void *stream);
+
 /* ---- allocation-free multiply (fp64 values, int32 row_ptr) ------------------
  * No counterpart in the reference. For callers that cannot allocate device
  * memory: code running inside an application that has already reserved the

@@ -40,7 +40,7 @@ EXPORTED = [
     "pf_mmio_read", "pf_free", "pf_shard_bounds_i32", "pf_shard_bounds_i64",
     "pf_gen_resolve", "pf_gen_count", "pf_gen_row_lengths_host", "pf_gen_rows_host",
     "pf_gen_x_host", "pf_gen_rows_device", "pf_gen_x_device",
-    "pf_spmv_noalloc_f64_i32",
+    "pf_spmv_noalloc_f64_i32", "pf_spmv_dist_f64_i64", "pf_spmv_dist_f64_i32",
 ]
 # the C++ drop-in symbols of include/PreFree.h (mangled)
 CXX_EXPORTED = [
@@ -82,6 +82,10 @@ def _load():
                  "pf_spmv_host_f32_i64"):
         f = getattr(lib, name)
         f.argtypes = [vp, i64, i64, i64, vp, vp, vp, dbl, vp, dbl, vp, vp]
+        f.restype = st
+    for name in ("pf_spmv_dist_f64_i64", "pf_spmv_dist_f64_i32"):
+        f = getattr(lib, name)
+        f.argtypes = [vp, i64, i64, i64, vp, vp, vp, vp, vp, C.c_int, C.c_int, vp, vp, i64, vp]
         f.restype = st
     lib.pf_spmv_noalloc_f64_i32.argtypes = [i64, i64, i64, vp, vp, vp, dbl, vp, dbl, vp, vp]
     lib.pf_spmv_noalloc_f64_i32.restype = st
@@ -194,6 +198,24 @@ def spmv(handle: Handle, m: int, n: int, nnz: int, row_ptr, col, val, x, y,
     f = getattr(lib, "pf_spmv_" + _suffix(vsz, isz))
     _check(f(handle.ptr, int(m), int(n), int(nnz), _ptr(row_ptr), _ptr(col), _ptr(val),
              float(alpha), _ptr(x), float(beta), _ptr(y), C.c_void_p(stream)))
+
+
+def spmv_dist(handle: Handle, m: int, n: int, nnz: int, row_ptr, col, val, x, prev_slots,
+              nranks: int, rank: int, out_ptrs_dev: int, slot_ptrs_dev: int, row_offset: int,
+              stream=None):
+    """Fused multiply + all-gather step (see pf_spmv_dist_* in prefree_b200.h):
+    this rank's rows of alpha*A*x go straight into every rank's next-x buffer
+    (out_ptrs_dev: device array of nranks pointers), ||y||^2 into every rank's
+    slot `rank` (slot_ptrs_dev); alpha = 1/sqrt(sum(prev_slots))."""
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream().cuda_stream
+    elif hasattr(stream, "cuda_stream"):
+        stream = stream.cuda_stream
+    f = lib.pf_spmv_dist_f64_i64 if row_ptr.element_size() == 8 else lib.pf_spmv_dist_f64_i32
+    _check(f(handle.ptr, int(m), int(n), int(nnz), _ptr(row_ptr), _ptr(col), _ptr(val), _ptr(x),
+             _ptr(prev_slots), int(nranks), int(rank), C.c_void_p(int(out_ptrs_dev)),
+             C.c_void_p(int(slot_ptrs_dev)), int(row_offset), C.c_void_p(stream)))
 
 
 def spmv_host(handle: Handle, row_ptr: np.ndarray, col: np.ndarray, val: np.ndarray,

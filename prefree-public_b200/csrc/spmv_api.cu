@@ -73,6 +73,10 @@ struct pf_handle_s {
   void *lx_buf = nullptr;
   size_t lx_bytes = 0;
   bool lx_dirty = false;
+  // fused all-gather: per-CTA norm partials + counter (zeroed when grown)
+  double *dist_part = nullptr;
+  unsigned *dist_counter = nullptr;
+  int64_t dist_cap = 0;
   pf::LongRowScratch lx{};
   // host-call buffers
   void *hbuf[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
@@ -119,6 +123,7 @@ static pf_status ensure_lx(pf_handle h, int64_t nnz, int64_t lt, cudaStream_t st
   const size_t total = b_hdr + b_ent + b_cnt + b_part;
   if (total > h->lx_bytes) {
     if (h->lx_buf) cudaFree(h->lx_buf);
+  if (h->dist_part) cudaFree(h->dist_part);
     h->lx_buf = nullptr;
     h->lx_bytes = 0;
     PF_CUDA_TRY(cudaMalloc(&h->lx_buf, total));
@@ -342,6 +347,77 @@ static pf_status launch_rowstream(pf_handle h, const SpmvParams<VT, IT> &prm, bo
   }
   PF_CUDA_TRY(cudaGetLastError());
   return PF_OK;
+}
+
+template <typename IT, int V>
+static pf_status launch_rowvec_dist(pf_handle h, const SpmvParams<double, IT> &prm,
+                                    const DistOut &D, cudaStream_t st) {
+  // 3 CTAs per SM: the fused epilogue's extra state spills at 4 (64 registers)
+  constexpr int U = 2, NTB = 256, MINB = 3;
+  const int64_t rows_per_block = (int64_t)(NTB / 32) * (32 / V) * U;
+  const int64_t want = ceil_div(prm.m, rows_per_block);
+  const int64_t cap = (int64_t)h->num_sms * 16;
+  const int64_t grid = std::max<int64_t>(1, std::min(want, cap));
+  if (grid > h->dist_cap) {
+    if (h->dist_part) cudaFree(h->dist_part);
+    h->dist_part = nullptr;
+    h->dist_cap = 0;
+    PF_CUDA_TRY(cudaMalloc(&h->dist_part, sizeof(double) * (size_t)grid + 256));
+    h->dist_counter = (unsigned *)(h->dist_part + grid);
+    PF_CUDA_TRY(cudaMemsetAsync(h->dist_counter, 0, sizeof(unsigned), st));
+    h->dist_cap = grid;
+  }
+  DistOut d = D;
+  d.cta_part = h->dist_part;
+  d.counter = h->dist_counter;
+  spmv_rowvec_kernel<double, IT, V, U, NTB, false, MINB, true>
+      <<<(unsigned)grid, NTB, 0, st>>>(prm, LongRowScratch{}, INT64_MAX, kLxChunk, d);
+  count_launch();
+  PF_CUDA_TRY(cudaGetLastError());
+  return PF_OK;
+}
+
+template <typename IT>
+static pf_status launch_dist(pf_handle h, int64_t m, int64_t n, int64_t nnz, const IT *row_ptr,
+                             const int32_t *col, const double *val, const double *x,
+                             const double *prev, int nranks, int rank, double *const *outs,
+                             double *const *slots, int64_t row_offset, cudaStream_t st) {
+  PF_CHECK_ARG(h != nullptr, "null handle");
+  PF_CHECK_ARG(m > 0 && n > 0 && nnz > 0, "empty shard");
+  PF_CHECK_ARG(row_ptr && col && val && x && prev && outs && slots, "null pointer");
+  PF_CHECK_ARG(nranks >= 1 && nranks <= 64 && rank >= 0 && rank < nranks, "bad rank/nranks");
+  PF_CHECK_ARG(sizeof(IT) == 8 || nnz <= INT32_MAX, "int32 row_ptr cannot index nnz");
+  PF_CHECK_ARG((((uintptr_t)col | (uintptr_t)val) & 15) == 0 && ((uintptr_t)row_ptr % sizeof(IT)) == 0 &&
+                   ((uintptr_t)x % 8) == 0,
+               "the fused multiply needs 16-byte aligned col/val");
+  int cur = 0;
+  PF_CUDA_TRY(cudaGetDevice(&cur));
+  PF_CHECK_ARG(cur == h->device, "handle bound to device %d, current device is %d", h->device, cur);
+  SpmvParams<double, IT> prm{};
+  prm.m = m;
+  prm.n = n;
+  prm.nnz = nnz;
+  prm.row_ptr = row_ptr;
+  prm.col = col;
+  prm.val = val;
+  prm.x = x;
+  prm.y = nullptr;
+  prm.alpha = 1.0;
+  prm.beta = 0.0;
+  prm.err = h->err;
+  DistOut D{};
+  D.outs = outs;
+  D.slots = slots;
+  D.prev = prev;
+  D.row_offset = row_offset;
+  D.nranks = nranks;
+  D.rank = rank;
+  switch (rowvec_lanes((double)nnz / (double)m)) {
+    case 2: return launch_rowvec_dist<IT, 2>(h, prm, D, st);
+    case 4: return launch_rowvec_dist<IT, 4>(h, prm, D, st);
+    case 8: return launch_rowvec_dist<IT, 8>(h, prm, D, st);
+    default: return launch_rowvec_dist<IT, 16>(h, prm, D, st);
+  }
 }
 
 template <typename VT, typename IT>
@@ -576,6 +652,7 @@ pf_status pf_handle_destroy(pf_handle h) {
   for (int i = 0; i < 5; ++i)
     if (h->hbuf[i]) cudaFree(h->hbuf[i]);
   if (h->lx_buf) cudaFree(h->lx_buf);
+  if (h->dist_part) cudaFree(h->dist_part);
   if (h->sample_dev) cudaFree(h->sample_dev);
   if (h->sample_host) cudaFreeHost(h->sample_host);
   cudaSetDevice(cur);
@@ -628,6 +705,24 @@ pf_status pf_handle_device_error(pf_handle h, uint32_t *bits, int clear) {
     return host_spmv<VT, IT>(h, m, n, nnz, row_ptr, col_idx, val, alpha, x,    \
                              beta, y, (cudaStream_t)stream);                   \
   }
+
+pf_status pf_spmv_dist_f64_i64(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                               const int64_t *row_ptr, const int32_t *col_idx,
+                               const double *val, const double *x, const double *prev_slots,
+                               int nranks, int rank, double *const *out_ptrs,
+                               double *const *slot_ptrs, int64_t row_offset, void *stream) {
+  return launch_dist<int64_t>(h, m, n, nnz, row_ptr, col_idx, val, x, prev_slots, nranks, rank,
+                              out_ptrs, slot_ptrs, row_offset, (cudaStream_t)stream);
+}
+
+pf_status pf_spmv_dist_f64_i32(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                               const int32_t *row_ptr, const int32_t *col_idx,
+                               const double *val, const double *x, const double *prev_slots,
+                               int nranks, int rank, double *const *out_ptrs,
+                               double *const *slot_ptrs, int64_t row_offset, void *stream) {
+  return launch_dist<int32_t>(h, m, n, nnz, row_ptr, col_idx, val, x, prev_slots, nranks, rank,
+                              out_ptrs, slot_ptrs, row_offset, (cudaStream_t)stream);
+}
 
 PF_DEFINE_SPMV(f64_i32, double, int32_t)
 PF_DEFINE_SPMV(f64_i64, double, int64_t)

@@ -57,6 +57,22 @@ struct LongRowEntry {
   int64_t row, s, e, base;  // row, its non-zero range, first chunk id
 };
 
+// Fused all-gather for the row-sharded iterated multiply: instead of y, each
+// finished row is stored straight into every rank's next-x buffer (peer
+// pointers over NVLink), and ||y||^2 of this rank's rows is reduced in the
+// same kernel and written to slot `rank` of every rank's norm-slot array.
+// alpha is taken on the device from the previous iteration's slots:
+// alpha = 1 / sqrt(sum of prev[0..nranks)).
+struct DistOut {
+  double *const *outs;   // [nranks] next-x base pointers (row index: row_offset + r)
+  double *const *slots;  // [nranks] norm-slot arrays (this rank writes index `rank`)
+  const double *prev;    // this rank's copy of the previous iteration's slots
+  double *cta_part;      // [grid] per-CTA partials
+  unsigned *counter;     // zero between launches
+  int64_t row_offset;
+  int nranks, rank;
+};
+
 struct LongRowScratch {
   unsigned long long *alloc;  // high 32 bits: entries, low 32 bits: chunks
   LongRowEntry *ent;          // [cap_entries], in chunk-base order

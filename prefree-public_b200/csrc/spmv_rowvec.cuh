@@ -55,10 +55,51 @@ struct Block4<float> {
 // lane 0 of its group lists it (one 64-bit atomic reserves a list slot and
 // its chunk ids in one step, so list order = chunk-base order) and
 // spmv_longrow_chunks_kernel finishes it.
-template <typename VT, typename IT, int V, int U, int NTB, bool LX, int MINB = 1>
+// DIST: the fused all-gather epilogue of DistOut (fp64 only).
+// ||y||^2 of the CTA in a fixed order (warp shuffles, then warps in order),
+// one partial per CTA; the last CTA to finish sums the partials in CTA order
+// and writes the total to slot `rank` of every rank's slots. The same bits on
+// every run, whatever the CTA finishing order.
+template <int NTB>
+__device__ __forceinline__ void dist_norm_epilogue(const DistOut &D, double nsq) {
+  __shared__ double part[NTB / 32];
+  __shared__ bool last;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __threadfence_system();  // this thread's stores to peers before the count
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) nsq += __shfl_xor_sync(0xffffffffu, nsq, d);
+  if (lane == 0) part[warp] = nsq;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < NTB / 32; ++w) t += part[w];
+    D.cta_part[blockIdx.x] = t;
+    __threadfence();
+    last = atomicAdd(D.counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // strided partial sums in a fixed order, then the same fixed tree
+  double t = 0.0;
+  for (unsigned b = threadIdx.x; b < gridDim.x; b += NTB) t += __ldcg(D.cta_part + b);
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) t += __shfl_xor_sync(0xffffffffu, t, d);
+  if (lane == 0) part[warp] = t;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double tot = 0.0;
+    for (int w = 0; w < NTB / 32; ++w) tot += part[w];
+    for (int p = 0; p < D.nranks; ++p) D.slots[p][D.rank] = tot;
+    *D.counter = 0;
+  }
+  __threadfence_system();
+}
+
+template <typename VT, typename IT, int V, int U, int NTB, bool LX, int MINB = 1, bool DIST = false>
 __global__ void __launch_bounds__(NTB, MINB)
 spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t lt,
-                   int64_t chunk) {
+                   int64_t chunk, const DistOut D = DistOut{}) {
   constexpr int GPW = 32 / V;  // row groups per warp
   constexpr int64_t RPW = (int64_t)GPW * U;
   const int lane = threadIdx.x & 31;
@@ -67,8 +108,20 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
   const int64_t warp_global = (blockIdx.x * (int64_t)NTB + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * NTB) >> 5;
   const int64_t stride = nwarps * RPW;
-  const double alpha = P.alpha, beta = P.beta;
+  double alpha = P.alpha;
+  const double beta = P.beta;
   const uint32_t n = (uint32_t)(P.n < 0xffffffffLL ? P.n : 0xffffffffLL);
+  double nsq = 0.0;  // DIST: this thread's share of ||y||^2
+  // DIST: the ranks' next-x pointers, read once per CTA (a row store must not
+  // wait on a pointer load)
+  __shared__ double *s_outs[DIST ? 64 : 1];
+  if (DIST) {
+    double s = 0.0;
+    for (int i = 0; i < D.nranks; ++i) s += D.prev[i];
+    alpha = s > 0.0 ? 1.0 / sqrt(s) : 1.0;
+    if (threadIdx.x < D.nranks) s_outs[threadIdx.x] = D.outs[threadIdx.x] + D.row_offset;
+    __syncthreads();
+  }
 
   int64_t rb = warp_global * RPW;
   int64_t s[U], e[U];
@@ -154,9 +207,15 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
       for (int u = 0; u < U; ++u) {
         const int64_t r = rb + (int64_t)u * GPW + gw;
         if (r < P.m && !skip[u]) {
-          double out = alpha * acc[u];
-          if (beta != 0.0) out += beta * (double)P.y[r];
-          P.y[r] = (VT)out;
+          if (DIST) {
+            const double out = alpha * acc[u];
+            nsq += out * out;
+            for (int p = 0; p < D.nranks; ++p) s_outs[p][r] = out;
+          } else {
+            double out = alpha * acc[u];
+            if (beta != 0.0) out += beta * (double)P.y[r];
+            P.y[r] = (VT)out;
+          }
         }
       }
     }
@@ -166,6 +225,7 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
       e[u] = ne[u];
     }
   }
+  if (DIST) dist_norm_epilogue<NTB>(D, nsq);
 }
 
 // Chunks of the listed long rows: warps take 1024-non-zero chunks

@@ -97,3 +97,84 @@ class PowerIteration:
         nsq = float(sq.item())
         self.alpha = 1.0 / math.sqrt(nsq) if nsq > 0 else 1.0
         return StepStats(nsq)
+
+
+class FusedPowerIteration:
+    """x_{k+1} = A x_k / ||A x_k|| with the all-gather fused into the multiply.
+
+    The kernel (pf_spmv_dist_*) stores every finished row of this rank
+    straight into every rank's next-x buffer over NVLink and reduces ||y||^2
+    in the same pass; alpha = 1/||x_k|| is taken on the device from the norm
+    slots, so a step is one kernel plus one cross-rank barrier and the host
+    never waits for the GPU.
+
+    Buffers: one symmetric-memory allocation per rank (torch symmetric
+    memory: every rank can address every other rank's copy) holding two x
+    buffers and two norm-slot arrays, used alternately: step k reads x[k%2]
+    and slots[k%2], writes x[(k+1)%2] and slots[(k+1)%2] on every rank. The
+    barrier after each step makes peers' stores visible and keeps any rank
+    from overwriting a buffer that another rank still reads. With one rank
+    the buffers are ordinary device memory and no barrier is needed.
+    """
+
+    SLOTS = 64
+
+    def __init__(self, pf, handle, row_ptr, col, val, x0, bounds, rank: int, world: int,
+                 group=None, stream=None):
+        import torch
+        self.torch, self.pf, self.h = torch, pf, handle
+        self.rp, self.col, self.val = row_ptr, col, val
+        self.rank, self.world = rank, world
+        self.n = int(x0.numel())
+        self.m = int(bounds[rank + 1] - bounds[rank])
+        self.row_offset = int(bounds[rank])
+        self.nnz = int(col.numel())
+        self.stream = stream or torch.cuda.current_stream(x0.device)
+        dev = x0.device
+        total = 2 * self.n + 2 * self.SLOTS
+        if world > 1:
+            import torch.distributed as dist
+            import torch.distributed._symmetric_memory as symm_mem
+            self.buf = symm_mem.empty(total, dtype=torch.float64, device=dev)
+            g = group or dist.group.WORLD
+            self.hdl = symm_mem.rendezvous(self.buf, g)
+            bases = [int(p) for p in self.hdl.buffer_ptrs]
+        else:
+            self.buf = torch.empty(total, dtype=torch.float64, device=dev)
+            self.hdl = None
+            bases = [self.buf.data_ptr()]
+        self.xs = [self.buf[0:self.n], self.buf[self.n:2 * self.n]]
+        self.slots = [self.buf[2 * self.n:2 * self.n + self.SLOTS],
+                      self.buf[2 * self.n + self.SLOTS:2 * self.n + 2 * self.SLOTS]]
+        self.out_ptrs = [torch.tensor([b + 8 * k * self.n for b in bases], dtype=torch.int64,
+                                      device=dev) for k in (0, 1)]
+        self.slot_ptrs = [torch.tensor([b + 8 * (2 * self.n + k * self.SLOTS) for b in bases],
+                                       dtype=torch.int64, device=dev) for k in (0, 1)]
+        self.xs[0].copy_(x0)
+        self.slots[0].zero_()
+        self.slots[1].zero_()
+        self.slots[0][0] = torch.dot(x0, x0)       # every rank holds the full x0
+        self.k = 0
+        torch.cuda.synchronize(dev)
+        if self.hdl is not None:
+            self.hdl.barrier(channel=0)
+
+    def step(self):
+        k = self.k
+        self.pf.spmv_dist(self.h, self.m, self.n, self.nnz, self.rp, self.col, self.val,
+                          self.xs[k % 2], self.slots[k % 2], self.world, self.rank,
+                          self.out_ptrs[(k + 1) % 2].data_ptr(),
+                          self.slot_ptrs[(k + 1) % 2].data_ptr(), self.row_offset,
+                          stream=self.stream)
+        if self.hdl is not None:
+            self.hdl.barrier(channel=0)
+        self.k += 1
+
+    @property
+    def x(self):
+        """The current (unnormalised) iterate."""
+        return self.xs[self.k % 2]
+
+    def norm_sq(self) -> float:
+        """||A x_{k-1}||^2 of the last step (synchronizes)."""
+        return float(self.slots[self.k % 2][:self.world].sum().item())

@@ -1,0 +1,143 @@
+"""Row-sharded iterated multiply on GPUs: the fused multiply + all-gather
+(pf_spmv_dist_*: rows stored straight into every rank's next x, ||y||^2
+reduced in the kernel) against the unfused path (pf_spmv + NCCL all-gather)
+and against the CPU oracle's power iteration. The 2-GPU case spawns NCCL
+ranks and is skipped when fewer than two GPUs are visible."""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+STEPS = 5
+
+
+def small_spec(pf):
+    return pf.GenSpec(cfg=5, seed=77, m=1 << 15, n=1 << 15)
+
+
+def oracle_iterates(pf, oracle, spec, steps):
+    rp, col, val = pf.gen_rows_host(spec)
+    x = pf.gen_x_host(spec)
+    norms = []
+    alpha = 1.0 / np.sqrt(x @ x)
+    for _ in range(steps):
+        y = alpha * oracle.serial(rp, col, val, x)
+        nsq = float(y @ y)
+        norms.append(nsq)
+        x, alpha = y, 1.0 / np.sqrt(nsq)
+    return x, norms
+
+
+def close(a, b, tol=1e-12):
+    return np.abs(a - b).max() <= tol * np.abs(b).max()
+
+
+def test_fused_one_gpu_matches_unfused_and_oracle(pf, oracle):
+    import torch
+    import importlib
+    pfd = importlib.import_module("prefree-public_b200.dist")
+    spec = small_spec(pf).resolved()
+    rp, col, val = pf.gen_rows_device(spec, index_dtype=torch.int64)
+    x0 = pf.gen_x_device(spec)
+    bounds = np.array([0, spec.m])
+    h = pf.Handle()
+    fused = pfd.FusedPowerIteration(pf, h, rp, col, val, x0, bounds, 0, 1)
+    nf = []
+    for _ in range(STEPS):
+        fused.step()
+        nf.append(fused.norm_sq())
+    y = torch.empty(spec.m, dtype=torch.float64, device="cuda")
+    x = x0.clone()
+
+    def local(xf, yl, alpha):
+        pf.spmv(h, spec.m, spec.n, col.numel(), rp, col, val, xf, yl, alpha, 0.0)
+
+    plain = pfd.PowerIteration(local, x, y, bounds, 0, 1)
+    nu = [plain.step().norm_sq for _ in range(STEPS)]
+    assert h.device_error() == 0
+    xr, nr = oracle_iterates(pf, oracle, spec, STEPS)
+    assert close(fused.x.cpu().numpy(), xr) and close(x.cpu().numpy(), xr)
+    assert np.allclose(nf, nr, rtol=1e-12) and np.allclose(nu, nr, rtol=1e-12)
+    # the fused kernel is deterministic
+    again = pfd.FusedPowerIteration(pf, h, rp, col, val, x0, bounds, 0, 1)
+    for _ in range(STEPS):
+        again.step()
+    assert torch.equal(again.x, fused.x)
+    h.close()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, q):
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), NCCL_NVLS_ENABLE="0")
+    import importlib
+    from datetime import timedelta
+    import torch
+    import torch.distributed as dist
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        pf = importlib.import_module("prefree-public_b200")
+        pfd = importlib.import_module("prefree-public_b200.dist")
+        spec = small_spec(pf).resolved()
+        b = pfd.gen_bounds(pf, spec, world)
+        r0, r1 = int(b[rank]), int(b[rank + 1])
+        rp, col, val = pf.gen_rows_device(spec, r0, r1, index_dtype=torch.int64, device=dev)
+        x0 = pf.gen_x_device(spec, device=dev)
+        h = pf.Handle()
+        fused = pfd.FusedPowerIteration(pf, h, rp, col, val, x0, b, rank, world)
+        nf = []
+        for _ in range(STEPS):
+            fused.step()
+            nf.append(fused.norm_sq())
+        x = x0.clone()
+        y = torch.empty(r1 - r0, dtype=torch.float64, device=dev)
+
+        def local(xf, yl, alpha):
+            pf.spmv(h, r1 - r0, spec.n, col.numel(), rp, col, val, xf, yl, alpha, 0.0)
+
+        plain = pfd.PowerIteration(local, x, y, b, rank, world)
+        nu = [plain.step().norm_sq for _ in range(STEPS)]
+        torch.cuda.synchronize()
+        q.put((rank, "ok", fused.x.cpu().numpy(), x.cpu().numpy(), nf, nu, h.device_error()))
+        del fused
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, "error", repr(e), None, None, None, None))
+
+
+def test_two_gpus_fused_and_nccl_match_oracle(pf, oracle):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    [p.start() for p in ps]
+    res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
+    [p.join(timeout=60) for p in ps]
+    for p in ps:
+        if p.is_alive():
+            p.kill()
+    assert all(r[1] == "ok" for r in res), res
+    xr, nr = oracle_iterates(pf, oracle, small_spec(pf), STEPS)
+    for rank, _, xf, xu, nf, nu, err in res:
+        assert err == 0
+        assert close(xf, xr) and close(xu, xr), rank
+        assert np.allclose(nf, nr, rtol=1e-12) and np.allclose(nu, nr, rtol=1e-12)
+    assert np.array_equal(res[0][2], res[1][2])       # every rank holds the same x
