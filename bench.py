@@ -54,54 +54,58 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+    """SM clocks and throttle reasons of one GPU, polled through NVML every
+    5 ms on a background thread while the timed region runs (read-only
+    queries). Falls back to an `nvidia-smi -lms` subprocess without NVML."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4}
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
+    def __init__(self, gpu_index: int, period_s: float = 0.005):
+        self.gpu, self.period = gpu_index, period_s
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._thread = None
+
+    def _poll(self, nv, hdl):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(float(nv.nvmlDeviceGetClockInfo(hdl, nv.NVML_CLOCK_SM)))
+                get = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    nv.nvmlDeviceGetCurrentClocksThrottleReasons
+                bits = get(hdl)
+                for name, b in self.REASONS.items():
+                    if bits & b:
+                        self.reasons.add(name)
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(self.period)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml as nv
+            import torch
+            nv.nvmlInit()
+            # NVML numbers GPUs in its own order: find this CUDA device by PCI id
+            p = torch.cuda.get_device_properties(self.gpu)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            hdl = nv.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(hdl, nv.NVML_CLOCK_SM))
+            self._thread = threading.Thread(target=self._poll, args=(nv, hdl), daemon=True)
+            self._thread.start()
+        except Exception:  # noqa: BLE001
+            self._thread = None
         return self
 
     def __exit__(self, *a):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for l in getattr(self, "lines", []):
-            f = [x.strip() for x in l.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for nm, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "samples": len(sm), "reasons": sorted(reasons)}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "samples": len(self.samples),
+                "reasons": sorted(self.reasons), "source": "NVML, 5 ms polling"}
 
 
 def traffic_per_row():
@@ -243,7 +247,8 @@ def main():
     ap.add_argument("--config", default="1,2,3,4,5", help="kernel mode: configs")
     ap.add_argument("--dtype", default="f64", help="kernel mode: f64 and/or f32")
     ap.add_argument("--variant", type=int, default=0, help="kernel mode: 0 auto, 1-4 forced")
-    ap.add_argument("--rows", type=int, default=0, help="kernel mode: override m")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="override m (kernel mode; power mode: profiling slice of config 5)")
     ap.add_argument("--cols", type=int, default=0, help="kernel mode: override n")
     ap.add_argument("--int64", action="store_true", help="kernel mode: int64 row_ptr")
     args = ap.parse_args()
@@ -272,6 +277,10 @@ def main():
     pfd = importlib.import_module("prefree-public_b200.dist")
 
     spec = pf.GenSpec(cfg=5, seed=SEED).resolved()
+    if args.rows:
+        # profiling case only: the first `rows` rows of config 5 (x keeps all
+        # 2^26 columns, so the gathers behave as in the full matrix)
+        spec = pf.GenSpec(cfg=5, seed=SEED, m=args.rows, n=spec.n).resolved()
     bounds = pfd.gen_bounds(pf, spec, world)
     r0, r1 = int(bounds[rank]), int(bounds[rank + 1])
     m_loc, n = r1 - r0, spec.n
