@@ -102,12 +102,26 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
                    int64_t chunk, const DistOut D = DistOut{}) {
   constexpr int GPW = 32 / V;  // row groups per warp
   constexpr int64_t RPW = (int64_t)GPW * U;
+  // DIST: a warp takes KS consecutive steps over 32 consecutive rows (a
+  // super-chunk), then jumps ahead by all warps' super-chunks, so that its 32
+  // results leave as one 256-byte store per rank instead of many small ones
+  // (small NVLink writes cap the all-gather near 150 GB/s per GPU). Without
+  // DIST a warp jumps after every step (KS = 1), which keeps every warp busy
+  // on matrices with few rows.
+  constexpr int KS = (!DIST || RPW >= 32) ? 1 : (int)(32 / RPW);
+  constexpr int64_t SUPER = RPW * KS;
   const int lane = threadIdx.x & 31;
   const int lig = lane & (V - 1);
   const int gw = lane / V;
+  const int wib = threadIdx.x >> 5;  // warp in block
   const int64_t warp_global = (blockIdx.x * (int64_t)NTB + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * NTB) >> 5;
   const int64_t stride = nwarps * RPW;
+  // first row of step k of this warp
+  auto step_row = [&](int64_t k) -> int64_t {
+    if (KS == 1) return warp_global * RPW + k * stride;
+    return ((k / KS) * nwarps + warp_global) * SUPER + (k % KS) * RPW;
+  };
   double alpha = P.alpha;
   const double beta = P.beta;
   const uint32_t n = (uint32_t)(P.n < 0xffffffffLL ? P.n : 0xffffffffLL);
@@ -115,6 +129,7 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
   // DIST: the ranks' next-x pointers, read once per CTA (a row store must not
   // wait on a pointer load)
   __shared__ double *s_outs[DIST ? 64 : 1];
+  __shared__ double s_wbuf[DIST ? NTB / 32 : 1][DIST ? SUPER : 1];  // a warp's super-chunk
   if (DIST) {
     double s = 0.0;
     for (int i = 0; i < D.nranks; ++i) s += D.prev[i];
@@ -123,7 +138,8 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
     __syncthreads();
   }
 
-  int64_t rb = warp_global * RPW;
+  int64_t kstep = 0;
+  int64_t rb = step_row(0);
   int64_t s[U], e[U];
 #pragma unroll
   for (int u = 0; u < U; ++u) {
@@ -131,11 +147,12 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
     s[u] = r < P.m ? (int64_t)__ldg(P.row_ptr + r) : 0;
     e[u] = r < P.m ? (int64_t)__ldg(P.row_ptr + r + 1) : 0;
   }
-  for (; rb < P.m; rb += stride) {
+  for (; rb < P.m; ++kstep, rb = (KS == 1 ? rb + stride : step_row(kstep))) {
+    const int64_t rbn = KS == 1 ? rb + stride : step_row(kstep + 1);
     int64_t ns[U], ne[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int64_t r = rb + stride + (int64_t)u * GPW + gw;
+      const int64_t r = rbn + (int64_t)u * GPW + gw;
       ns[u] = r < P.m ? (int64_t)__ldg(P.row_ptr + r) : 0;
       ne[u] = r < P.m ? (int64_t)__ldg(P.row_ptr + r + 1) : 0;
     }
@@ -210,7 +227,7 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
           if (DIST) {
             const double out = alpha * acc[u];
             nsq += out * out;
-            for (int p = 0; p < D.nranks; ++p) s_outs[p][r] = out;
+            s_wbuf[wib][(kstep % KS) * RPW + u * GPW + gw] = out;
           } else {
             double out = alpha * acc[u];
             if (beta != 0.0) out += beta * (double)P.y[r];
@@ -218,6 +235,18 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
           }
         }
       }
+    }
+    if (DIST && ((kstep % KS) == KS - 1 || rbn >= P.m)) {
+      // the super-chunk is complete (or this warp is done): one 256-byte
+      // store per rank (rows past m or not reached are not written)
+      __syncwarp();
+      const int64_t r0 = rb - (kstep % KS) * RPW;
+      const int64_t rows = min((int64_t)SUPER, min(P.m, rb + RPW) - r0);
+      for (int64_t i = lane; i < rows; i += 32) {
+        const double v = s_wbuf[wib][i];
+        for (int p = 0; p < D.nranks; ++p) s_outs[p][r0 + i] = v;
+      }
+      __syncwarp();
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
