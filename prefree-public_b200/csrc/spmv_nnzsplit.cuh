@@ -50,12 +50,54 @@ struct SpmvParams {
   unsigned *err;        // device error word
 };
 
-// Long-row escape list (ROWVEC_LX): rows longer than the short-row limit are
-// listed by the row kernel and finished by the chunk kernel. All counters are
-// zero between launches (the chunk kernel's last CTA resets them).
-struct LongRowEntry {
-  int64_t row, s, e, base;  // row, its non-zero range, first chunk id
+// Long-row escape (ROWVEC_LX, ROWSTREAM_LX): rows longer than the short-row
+// limit are cut into chunks of at most `chunk` non-zeros by the row kernel,
+// which writes one descriptor per chunk; the chunk kernel sums the chunks.
+// Chunk ids are reserved with a 64-bit atomic counter. All counters are zero
+// between launches (the chunk kernel's last CTA resets them).
+struct LongChunk {
+  int64_t row;    // the row
+  int64_t cs;     // first non-zero of the chunk
+  int64_t first;  // chunk id of the row's first chunk (partials, finish counter)
+  int32_t len;    // non-zeros in the chunk
+  int32_t nch;    // chunks of the row (1: the chunk writes y itself)
 };
+
+struct LongRowScratch {
+  unsigned long long *alloc;  // chunk ids reserved so far
+  LongChunk *chunks;          // [cap_chunks]
+  unsigned *cnt;              // [cap_chunks], at a row's first chunk id: chunks finished
+  double *part;               // [cap_chunks] chunk partials
+  unsigned *done;             // CTAs of the chunk kernel finished
+  int64_t cap_chunks;
+};
+
+__device__ __forceinline__ int64_t lx_num_chunks(int64_t s, int64_t e, int64_t chunk) {
+  return (e - s + chunk - 1) / chunk;
+}
+
+// Descriptors of chunks [0, nch) of row `row` = [s, e), first chunk id `first`,
+// written by `nthreads` cooperating threads (thread `t` of them).
+__device__ __forceinline__ void lx_write_chunks(const LongRowScratch &L, int64_t row, int64_t s,
+                                                int64_t e, int64_t first, int64_t chunk, int t,
+                                                int nthreads) {
+  const int64_t nch = lx_num_chunks(s, e, chunk);
+  for (int64_t c = t; c < nch; c += nthreads) {
+    const int64_t cs = s + c * chunk;
+    L.chunks[first + c] =
+        LongChunk{row, cs, first, (int32_t)min(chunk, e - cs), (int32_t)nch};
+  }
+}
+
+// One thread lists one row directly (one global atomic per row: for rare
+// rows, or when a CTA's shared list is full).
+__device__ __forceinline__ void lx_publish_row(const LongRowScratch &L, int64_t row, int64_t s,
+                                               int64_t e, int64_t chunk, unsigned *err) {
+  const int64_t nch = lx_num_chunks(s, e, chunk);
+  const int64_t first = (int64_t)atomicAdd(L.alloc, (unsigned long long)nch);
+  if (first + nch <= L.cap_chunks) lx_write_chunks(L, row, s, e, first, chunk, 0, 1);
+  else atomicOr(err, PF_DEVERR_ROWPTR);
+}
 
 // Fused all-gather for the row-sharded iterated multiply: instead of y, each
 // finished row is stored straight into every rank's next-x buffer (peer
@@ -73,15 +115,6 @@ struct DistOut {
   int nranks, rank;
 };
 
-struct LongRowScratch {
-  unsigned long long *alloc;  // high 32 bits: entries, low 32 bits: chunks
-  LongRowEntry *ent;          // [cap_entries], in chunk-base order
-  unsigned *ent_cnt;          // per entry: chunks finished
-  double *part;               // [cap_chunks] chunk partials
-  unsigned *next;             // next chunk to take
-  unsigned *done;             // CTAs finished
-  int64_t cap_entries, cap_chunks;
-};
 
 // Smallest idx in [0, m] with row_ptr[idx] >= key (row_ptr[m] >= key assumed).
 // One warp, 32 probes per step: ~log32(m) dependent loads.

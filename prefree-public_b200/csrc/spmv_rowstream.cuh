@@ -250,15 +250,7 @@ spmv_rowstream_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int rp
         re = rs;
         store = false;
       } else if (live && !staged && LX && len > lx_lt) {
-        if (lig == 0) {
-          const unsigned long long nch = (unsigned long long)((len + chunk - 1) / chunk);
-          const unsigned long long old = atomicAdd(L.alloc, (1ull << 32) | nch);
-          const int64_t idx = (int64_t)(old >> 32), base = (int64_t)(old & 0xffffffffull);
-          if (idx < L.cap_entries && base + (int64_t)nch <= L.cap_chunks)
-            L.ent[idx] = LongRowEntry{r0 + j, rs, re, base};
-          else
-            atomicOr(P.err, PF_DEVERR_ROWPTR);
-        }
+        if (lig == 0) lx_publish_row(L, r0 + j, rs, re, chunk, P.err);
         re = rs;
         store = false;
       }

@@ -52,9 +52,12 @@ struct Block4<float> {
 };
 
 // LX (long-row escape): a row longer than `lt` non-zeros is not summed here;
-// lane 0 of its group lists it (one 64-bit atomic reserves a list slot and
-// its chunk ids in one step, so list order = chunk-base order) and
-// spmv_longrow_chunks_kernel finishes it.
+// lane 0 of its group appends it to the CTA's list in shared memory, and at
+// the end the CTA reserves chunk ids for its whole list with one global
+// atomic and writes the chunk descriptors; spmv_longrow_chunks_kernel sums
+// them. (One global atomic per long row, all on one address, serialises: on a
+// power-law matrix with 40k long rows it cost ~150 us.) Rows beyond the
+// shared list's capacity are published one by one.
 // DIST: the fused all-gather epilogue of DistOut (fp64 only).
 // ||y||^2 of the CTA in a fixed order (warp shuffles, then warps in order),
 // one partial per CTA; the last CTA to finish sums the partials in CTA order
@@ -96,6 +99,45 @@ __device__ __forceinline__ void dist_norm_epilogue(const DistOut &D, double nsq)
   __threadfence_system();
 }
 
+// Publishes a CTA's shared list of long rows (called by every thread): one
+// global atomic reserves chunk ids for the whole list, in list order, then
+// warp 0 writes the chunk descriptors.
+__device__ __forceinline__ void lx_publish_list(const LongRowScratch &L, const int64_t (*lst)[3],
+                                                const unsigned *n_shared, int cap, int64_t chunk,
+                                                unsigned *err) {
+  __syncthreads();
+  const unsigned cnt = min(*n_shared, (unsigned)cap);
+  if (cnt == 0 || threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  int64_t tot = 0;
+  for (unsigned i = lane; i < cnt; i += 32) tot += lx_num_chunks(lst[i][1], lst[i][2], chunk);
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, d);
+  int64_t off = 0;
+  if (lane == 0) off = (int64_t)atomicAdd(L.alloc, (unsigned long long)tot);
+  off = __shfl_sync(0xffffffffu, off, 0);
+  if (off + tot > L.cap_chunks) {
+    if (lane == 0) atomicOr(err, PF_DEVERR_ROWPTR);
+    return;
+  }
+  for (unsigned i0 = 0; i0 < cnt; i0 += 32) {
+    const unsigned i = i0 + lane;
+    const int64_t nch = i < cnt ? lx_num_chunks(lst[i][1], lst[i][2], chunk) : 0;
+    int64_t inc = nch;  // inclusive scan over the batch
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int64_t t = __shfl_up_sync(0xffffffffu, inc, d);
+      if (lane >= d) inc += t;
+    }
+    const int64_t first = off + inc - nch;
+    for (unsigned j = 0; j < 32 && i0 + j < cnt; ++j) {
+      const int64_t fj = __shfl_sync(0xffffffffu, first, j);
+      lx_write_chunks(L, lst[i0 + j][0], lst[i0 + j][1], lst[i0 + j][2], fj, chunk, lane, 32);
+    }
+    off += __shfl_sync(0xffffffffu, inc, 31);
+  }
+}
+
 template <typename VT, typename IT, int V, int U, int NTB, bool LX, int MINB = 1, bool DIST = false>
 __global__ void __launch_bounds__(NTB, MINB)
 spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t lt,
@@ -128,6 +170,11 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
   double nsq = 0.0;  // DIST: this thread's share of ||y||^2
   // DIST: the ranks' next-x pointers, read once per CTA (a row store must not
   // wait on a pointer load)
+  constexpr int LXCAP = LX ? 256 : 1;
+  __shared__ int64_t s_lx[LXCAP][3];  // row, s, e
+  __shared__ unsigned s_lxn;
+  if (LX && threadIdx.x == 0) s_lxn = 0;
+  if (LX) __syncthreads();
   __shared__ double *s_outs[DIST ? 64 : 1];
   __shared__ double s_wbuf[DIST ? NTB / 32 : 1][DIST ? SUPER : 1];  // a warp's super-chunk
   if (DIST) {
@@ -166,14 +213,14 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
       if (LX && e[u] - s[u] > lt) {
         skip[u] = true;
         if (lig == 0) {
-          const unsigned long long nch = (unsigned long long)((e[u] - s[u] + chunk - 1) / chunk);
-          const unsigned long long old = atomicAdd(L.alloc, (1ull << 32) | nch);
-          const int64_t idx = (int64_t)(old >> 32);
-          const int64_t base = (int64_t)(old & 0xffffffffull);
-          if (idx < L.cap_entries && base + (int64_t)nch <= L.cap_chunks) {
-            L.ent[idx] = LongRowEntry{rb + (int64_t)u * GPW + gw, s[u], e[u], base};
+          const int64_t row = rb + (int64_t)u * GPW + gw;
+          const unsigned p = atomicAdd(&s_lxn, 1u);
+          if (p < (unsigned)LXCAP) {
+            s_lx[p][0] = row;
+            s_lx[p][1] = s[u];
+            s_lx[p][2] = e[u];
           } else {
-            atomicOr(P.err, PF_DEVERR_ROWPTR);
+            lx_publish_row(L, row, s[u], e[u], chunk, P.err);
           }
         }
         e[u] = s[u];  // nothing to sum here
@@ -255,79 +302,91 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
     }
   }
   if (DIST) dist_norm_epilogue<NTB>(D, nsq);
+  if (LX) lx_publish_list(L, s_lx, &s_lxn, LXCAP, chunk, P.err);
 }
 
-// Chunks of the listed long rows: warps take 1024-non-zero chunks
-// dynamically, sum them with 16-byte block loads, store the partial; the last
-// chunk of a row to finish sums the row's partials in chunk order (the same
-// order on every run) and writes y. The last CTA resets the counters.
-template <typename VT, typename IT, int NTB>
+// Chunks of the listed long rows: warp w sums chunks w, w + W, ... (W warps in
+// the grid; the next descriptor is loaded while the current chunk is summed),
+// with 16-byte block loads, UNR blocks per lane in flight. A row of one chunk
+// is written at once; otherwise the chunk stores its partial and the last of
+// the row's chunks to finish sums the partials in chunk order (the same order
+// on every run) and writes y. The last CTA resets the counters.
+template <typename VT, typename IT, int NTB, int UNR = 2>
 __global__ void __launch_bounds__(NTB)
-spmv_longrow_chunks_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t chunk) {
+spmv_longrow_chunks_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L) {
   const int lane = threadIdx.x & 31;
-  const unsigned long long a = *((volatile unsigned long long *)L.alloc);
-  const int64_t n_ent = (int64_t)(a >> 32);
-  const int64_t n_chunks = (int64_t)(a & 0xffffffffull);
+  const int64_t n_chunks = (int64_t)*((volatile unsigned long long *)L.alloc);
+  const int64_t warp = ((int64_t)blockIdx.x * NTB + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * NTB) >> 5;
   const uint32_t n = (uint32_t)(P.n < 0xffffffffLL ? P.n : 0xffffffffLL);
   bool bad = false;
-  while (n_chunks > 0) {
-    int64_t g = 0;
-    if (lane == 0) g = (int64_t)atomicAdd(L.next, 1u);
-    g = __shfl_sync(0xffffffffu, g, 0);
-    if (g >= n_chunks) break;
-    // entry with the largest base <= g
-    int64_t lo = 0, hi = n_ent - 1;
-    while (lo < hi) {
-      const int64_t mid = (lo + hi + 1) >> 1;
-      if (__ldcg(&L.ent[mid].base) <= g) lo = mid;
-      else hi = mid - 1;
-    }
-    const LongRowEntry E = L.ent[lo];
-    const int64_t k = g - E.base;
-    const int64_t cs = E.s + k * chunk;
-    const int64_t ce = min(cs + chunk, E.e);
+  LongChunk cur;
+  if (warp < n_chunks) cur = L.chunks[warp];
+  for (int64_t g = warp; g < n_chunks; g += nwarps) {
+    LongChunk nxt = cur;
+    if (g + nwarps < n_chunks) nxt = L.chunks[g + nwarps];
+    const int64_t cs = cur.cs, ce = cur.cs + cur.len;
     double acc = 0.0;
-    for (int64_t q = (cs & ~(int64_t)3) + 4 * lane; q < ce; q += 4 * 32) {
-      const int4 c4 = __ldcs(reinterpret_cast<const int4 *>(P.col + q));
-      VT v4[4];
-      Block4<VT>::load(P.val, q, q + 1 >= cs, q + 2 < ce, v4);
-      const int cc[4] = {c4.x, c4.y, c4.z, c4.w};
+    for (int64_t q0 = (cs & ~(int64_t)3) + 4 * lane; q0 < ce; q0 += 4 * 32 * UNR) {
+      int4 c4[UNR];
+      VT v4[UNR][4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int64_t el = q + i;
-        const bool use = el >= cs && el < ce;
-        const bool inb = (uint32_t)cc[i] < n;
-        bad |= use && !inb;
-        const VT xv = (use && inb) ? __ldg(P.x + cc[i]) : VT(0);
-        acc += (double)v4[i] * (double)xv;
+      for (int j = 0; j < UNR; ++j) {
+        const int64_t q = q0 + 4 * 32 * j;
+        const bool act = q < ce;
+        c4[j] = act ? __ldcs(reinterpret_cast<const int4 *>(P.col + q)) : make_int4(0, 0, 0, 0);
+        Block4<VT>::load(P.val, q, act && q + 1 >= cs, act && q + 2 < ce, v4[j]);
+      }
+      VT xv[UNR][4];
+#pragma unroll
+      for (int j = 0; j < UNR; ++j) {
+        const int64_t q = q0 + 4 * 32 * j;
+        const int cc[4] = {c4[j].x, c4[j].y, c4[j].z, c4[j].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const bool use = q + i >= cs && q + i < ce;
+          const bool inb = (uint32_t)cc[i] < n;
+          bad |= use && !inb;
+          xv[j][i] = (use && inb) ? __ldg(P.x + cc[i]) : VT(0);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < UNR; ++j) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc += (double)v4[j][i] * (double)xv[j][i];
       }
     }
 #pragma unroll
     for (int d = 16; d > 0; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d);
     if (lane == 0) {
-      L.part[g] = acc;
-      __threadfence();
-      const unsigned nch = (unsigned)((E.e - E.s + chunk - 1) / chunk);
-      const unsigned old = atomicAdd(&L.ent_cnt[lo], 1u);
-      if (old == nch - 1) {
+      if (cur.nch == 1) {
+        double out = P.alpha * acc;
+        if (P.beta != 0.0) out += P.beta * (double)P.y[cur.row];
+        P.y[cur.row] = (VT)out;
+      } else {
+        L.part[g] = acc;
         __threadfence();
-        double sum = 0.0;
-        for (unsigned c = 0; c < nch; ++c) sum += __ldcg(&L.part[E.base + c]);
-        double out = P.alpha * sum;
-        if (P.beta != 0.0) out += P.beta * (double)P.y[E.row];
-        P.y[E.row] = (VT)out;
-        L.ent_cnt[lo] = 0;
+        const unsigned old = atomicAdd(&L.cnt[cur.first], 1u);
+        if (old == (unsigned)cur.nch - 1) {
+          __threadfence();
+          double sum = 0.0;
+          for (int c = 0; c < cur.nch; ++c) sum += __ldcg(&L.part[cur.first + c]);
+          double out = P.alpha * sum;
+          if (P.beta != 0.0) out += P.beta * (double)P.y[cur.row];
+          P.y[cur.row] = (VT)out;
+          L.cnt[cur.first] = 0;
+        }
       }
     }
+    cur = nxt;
   }
   if (bad) atomicOr(P.err, PF_DEVERR_BOUNDS);
-  // last CTA out resets the work counters for the next launch
+  // last CTA out resets the chunk counter for the next launch
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
     const unsigned old = atomicAdd(L.done, 1u);
     if (old == gridDim.x - 1) {
-      *L.next = 0;
       *L.alloc = 0ull;
       *L.done = 0;
       __threadfence();
