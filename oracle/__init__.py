@@ -10,7 +10,11 @@ Two libraries:
     fp64/fp32 inputs, plus per-row |a*x| sums and a compensated sum;
   * ``_ref/libref.so`` — the reference's own ``spmv_serial`` and
     ``mmio_allinone`` (utilities/mmio.cpp:1547-1713), compiled from the
-    reference sources by oracle/Makefile.
+    reference sources by oracle/Makefile;
+  * ``_ref/libref_gpu.so`` — the reference's own GPU entry point
+    ``preFreeSpMV`` with its kernel (src/spmv_kernel/preFreeSpMV.cu),
+    compiled unmodified for sm_100a by oracle/Makefile: a second checker on
+    inputs it handles correctly, and the B200 timing comparison.
 The restatement is pinned to the reference build by tests/test_oracle.py
 (bit-identical outputs) and by the golden fixtures in tests/golden/ that the
 reference build produced (tests/golden/make_golden.py).
@@ -26,6 +30,10 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_LIB = os.path.join(_HERE, "liboracle.so")
 REF_LIB = os.path.join(_HERE, "_ref", "libref.so")
+REF_GPU_LIB = os.path.join(_HERE, "_ref", "libref_gpu.so")
+# include/PreFree.h:3-5 under -Dfp64: preFreeSpMV(double*, int*, int*, double*,
+# double*, int, int, int, double*, double*), C++ linkage
+REF_GPU_SYMBOL = "_Z11preFreeSpMVPdPiS0_S_S_iiiS_S_"
 
 _vp, _i64, _i32 = C.c_void_p, C.c_int64, C.c_int32
 
@@ -70,6 +78,44 @@ def ref_lib():
         r.ref_free.restype = None
         _ref = r
     return _ref
+
+
+_ref_gpu = None
+
+
+def ref_gpu_available() -> bool:
+    return os.path.exists(REF_GPU_LIB)
+
+
+def ref_gpu_prefree(val, row_ptr, col, x, m: int, n: int):
+    """The reference's own preFreeSpMV on the GPU (oracle/_ref/libref_gpu.so):
+    host fp64 CSR with int32 indices in, y = A*x out, with the reference's own
+    timings (ms per multiply over 4000 launches after 200 warm-ups, and ms of
+    its start-row pre-pass). Returns (y, cdTime, cdPre). The reference copies
+    row_ptr[0 .. m+1] (one entry past the CSR, src/spmv_kernel/preFreeSpMV.cu:580),
+    so it is handed a copy with one padding entry."""
+    global _ref_gpu
+    if _ref_gpu is None:
+        if not ref_gpu_available():
+            raise FileNotFoundError(f"{REF_GPU_LIB} not built (make -C oracle with the reference tree)")
+        r = C.CDLL(REF_GPU_LIB)
+        f = getattr(r, REF_GPU_SYMBOL)
+        f.argtypes = [_vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int,
+                      C.POINTER(C.c_double), C.POINTER(C.c_double)]
+        f.restype = None
+        _ref_gpu = f
+    nnz = int(row_ptr[m]) - int(row_ptr[0])
+    assert int(row_ptr[0]) == 0 and nnz < 2**31
+    rp = np.empty(m + 2, dtype=np.int32)
+    rp[:m + 1] = row_ptr
+    rp[m + 1] = row_ptr[m]
+    v = np.ascontiguousarray(val, dtype=np.float64)
+    c = np.ascontiguousarray(col, dtype=np.int32)
+    xx = np.ascontiguousarray(x, dtype=np.float64)
+    y = np.zeros(max(m, 1), dtype=np.float64)
+    t, pre = C.c_double(), C.c_double()
+    _ref_gpu(_p(v), _p(rp), _p(c), _p(xx), _p(y), m, n, nnz, C.byref(t), C.byref(pre))
+    return y[:m], t.value, pre.value
 
 
 def _p(a: np.ndarray) -> int:

@@ -40,6 +40,11 @@ enum : unsigned {
 
 // Count of our kernels launched since library load (bench reports it).
 extern unsigned long long g_launch_count;
+// spmv_api.cu: the one-time work of the first multiply with a matrix
+pf_status prepare_matrix_i32(pf_handle h, int64_t m, int64_t nnz, const int32_t *row_ptr,
+                             cudaStream_t st);
+pf_status prepare_matrix_i64(pf_handle h, int64_t m, int64_t nnz, const int64_t *row_ptr,
+                             cudaStream_t st);
 void count_launches(unsigned long long k);
 
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) {

@@ -2,8 +2,8 @@
 // (src/spmv_kernel/preFreeSpMV.cu:563-662) on top of the device-pointer core.
 //
 // Sequence, as in the reference: allocate device arrays, copy CSR + x in,
-// run the pre-pass (here: the host-side variant choice, timed into *cdPre —
-// there is no preprocessing kernel), 200 warm-up + 4000 timed launches on the
+// run the pre-pass (here: the variant choice from sampled row lengths, wall
+// time into *cdPre, once per call), 200 warm-up + 4000 timed launches on the
 // legacy default stream timed with events (*cdTime = ms per launch), one clean
 // multiply, copy y out, free. Unlike the reference, every launch of the timed
 // loop computes the same correct y (alpha = 1, beta = 0 overwrites y), failures
@@ -107,9 +107,15 @@ static pf_status prefree_impl(VT *csrVal, IT *csrRowPtr, int32_t *csrColInd,
   }
   if (n > 0) PF_TRY_CLEAN(cudaMemcpy(d_x, X_val, sizeof(VT) * n, cudaMemcpyHostToDevice));
 
-  // pre-pass: variant choice from O(1) row_ptr statistics (host)
+  // pre-pass: variant choice from sampled row lengths
+  PF_TRY_CLEAN(cudaDeviceSynchronize());
   const auto t0 = std::chrono::steady_clock::now();
   pf_handle_set_variant(h, PF_VARIANT_AUTO);
+  if (sizeof(IT) == 8)
+    st = prepare_matrix_i64(h, m, nnz, reinterpret_cast<const int64_t *>(d_rp), nullptr);
+  else
+    st = prepare_matrix_i32(h, m, nnz, reinterpret_cast<const int32_t *>(d_rp), nullptr);
+  if (st != PF_OK) { cleanup(); return st; }
   const auto t1 = std::chrono::steady_clock::now();
   *cdPre = std::chrono::duration<double, std::milli>(t1 - t0).count();
 

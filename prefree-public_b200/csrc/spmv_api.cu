@@ -626,6 +626,30 @@ static pf_status launch_warpsplit(pf_handle h, SpmvParams<VT, IT> prm, cudaStrea
   return PF_OK;
 }
 
+// The one-time work of the first multiply with a matrix: the variant choice
+// from sampled row lengths (cached in the handle). Leaves the stream
+// synchronised.
+template <typename IT>
+static pf_status prepare_matrix(pf_handle h, int64_t m, int64_t nnz, const IT *row_ptr,
+                                cudaStream_t st) {
+  PF_CHECK_ARG(h != nullptr, "null handle");
+  if (m <= 0 || nnz <= 0) return PF_OK;
+  pf_variant_choice ch;
+  pf_status s = select_variant<IT>(h, m, nnz, row_ptr, st, &ch);
+  if (s != PF_OK) return s;
+  PF_CUDA_TRY(cudaStreamSynchronize(st));
+  return PF_OK;
+}
+
+pf_status prepare_matrix_i32(pf_handle h, int64_t m, int64_t nnz, const int32_t *row_ptr,
+                             cudaStream_t st) {
+  return prepare_matrix<int32_t>(h, m, nnz, row_ptr, st);
+}
+pf_status prepare_matrix_i64(pf_handle h, int64_t m, int64_t nnz, const int64_t *row_ptr,
+                             cudaStream_t st) {
+  return prepare_matrix<int64_t>(h, m, nnz, row_ptr, st);
+}
+
 // Host-buffer call: copy in, one multiply, copy out.
 template <typename VT, typename IT>
 static pf_status host_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
