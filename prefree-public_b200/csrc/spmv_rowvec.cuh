@@ -187,56 +187,72 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
 
   int64_t kstep = 0;
   int64_t rb = step_row(0);
-  int64_t s[U], e[U];
+  // row bounds kept in row_ptr's own type (half the registers for int32)
+  IT s[U], e[U];
 #pragma unroll
   for (int u = 0; u < U; ++u) {
     const int64_t r = rb + (int64_t)u * GPW + gw;
-    s[u] = r < P.m ? (int64_t)__ldg(P.row_ptr + r) : 0;
-    e[u] = r < P.m ? (int64_t)__ldg(P.row_ptr + r + 1) : 0;
+    s[u] = r < P.m ? __ldg(P.row_ptr + r) : IT(0);
+    e[u] = r < P.m ? __ldg(P.row_ptr + r + 1) : IT(0);
   }
   for (; rb < P.m; ++kstep, rb = (KS == 1 ? rb + stride : step_row(kstep))) {
     const int64_t rbn = KS == 1 ? rb + stride : step_row(kstep + 1);
-    int64_t ns[U], ne[U];
+    IT ns[U], ne[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t r = rbn + (int64_t)u * GPW + gw;
-      ns[u] = r < P.m ? (int64_t)__ldg(P.row_ptr + r) : 0;
-      ne[u] = r < P.m ? (int64_t)__ldg(P.row_ptr + r + 1) : 0;
+      ns[u] = r < P.m ? __ldg(P.row_ptr + r) : IT(0);
+      ne[u] = r < P.m ? __ldg(P.row_ptr + r + 1) : IT(0);
     }
+    // each row from the 16-byte block q0 holding its first non-zero, with
+    // 32-bit offsets from it (rows longer than 2^31 - 8 non-zeros are flagged,
+    // not summed)
     double acc[U];
-    int64_t q[U];
+    int64_t q0[U];
+    int o[U], lo[U], len[U];
     bool skip[U];
+    bool bad = false;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       acc[u] = 0.0;
       skip[u] = false;
-      if (LX && e[u] - s[u] > lt) {
+      if (LX && (int64_t)e[u] - (int64_t)s[u] > lt) {
         skip[u] = true;
         if (lig == 0) {
           const int64_t row = rb + (int64_t)u * GPW + gw;
           const unsigned p = atomicAdd(&s_lxn, 1u);
           if (p < (unsigned)LXCAP) {
             s_lx[p][0] = row;
-            s_lx[p][1] = s[u];
-            s_lx[p][2] = e[u];
+            s_lx[p][1] = (int64_t)s[u];
+            s_lx[p][2] = (int64_t)e[u];
           } else {
-            lx_publish_row(L, row, s[u], e[u], chunk, P.err);
+            lx_publish_row(L, row, (int64_t)s[u], (int64_t)e[u], chunk, P.err);
           }
         }
         e[u] = s[u];  // nothing to sum here
       }
-      q[u] = (s[u] & ~(int64_t)3) + 4 * lig;
+      q0[u] = (int64_t)s[u] & ~(int64_t)3;
+      lo[u] = (int)((int64_t)s[u] - q0[u]);
+      const int64_t l64 = (int64_t)e[u] - q0[u];
+      if (l64 > (int64_t)INT32_MAX - 8) {
+        if (lig == 0) atomicOr(P.err, PF_DEVERR_ROWPTR);
+        skip[u] = true;
+        len[u] = 0;
+      } else {
+        len[u] = (int)l64;
+      }
+      o[u] = 4 * lig;
     }
-    bool bad = false;
     bool more = true;
     while (more) {
       int4 c4[U];
       VT v4[U][4];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        const bool act = q[u] < e[u];
-        c4[u] = act ? __ldcs(reinterpret_cast<const int4 *>(P.col + q[u])) : make_int4(0, 0, 0, 0);
-        Block4<VT>::load(P.val, q[u], act && q[u] + 1 >= s[u], act && q[u] + 2 < e[u], v4[u]);
+        const bool act = o[u] < len[u];
+        const int64_t q = q0[u] + o[u];
+        c4[u] = act ? __ldcs(reinterpret_cast<const int4 *>(P.col + q)) : make_int4(0, 0, 0, 0);
+        Block4<VT>::load(P.val, q, act && o[u] + 1 >= lo[u], act && o[u] + 2 < len[u], v4[u]);
       }
       VT xv[U][4];
 #pragma unroll
@@ -244,8 +260,8 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
         const int cc[4] = {c4[u].x, c4[u].y, c4[u].z, c4[u].w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int64_t el = q[u] + i;
-          const bool use = el >= s[u] && el < e[u];
+          const int el = o[u] + i;
+          const bool use = el >= lo[u] && el < len[u];
           const bool inb = (uint32_t)cc[i] < n;
           bad |= use && !inb;
           xv[u][i] = (use && inb) ? __ldg(P.x + cc[i]) : VT(0);
@@ -256,8 +272,8 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
       for (int u = 0; u < U; ++u) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[u] += (double)v4[u][i] * (double)xv[u][i];
-        q[u] += 4 * V;
-        more |= q[u] < e[u];
+        o[u] += 4 * V;
+        more |= o[u] < len[u];
       }
     }
     if (bad) atomicOr(P.err, PF_DEVERR_BOUNDS);
