@@ -106,7 +106,9 @@ static pf_status ensure_scratch(pf_handle h, int64_t num_ctas, cudaStream_t st) 
   return PF_OK;
 }
 
-constexpr int64_t kLxChunk = 512;  // non-zeros per long-row chunk
+// non-zeros per long-row chunk: the window spmv_longrow_chunks_kernel covers
+// in one pass (128 * its UNR)
+constexpr int64_t kLxChunk = 512;
 
 static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
 
@@ -218,8 +220,9 @@ static pf_variant_choice choose_from_stats(int64_t m, int64_t nnz, const int64_t
   for (int i = 0; i < S; ++i) mx = std::max(mx, sample[i]);
   pf_variant_choice ch;
   // regular rows (the sample never strays far above the mean): whole rows per
-  // lane group; otherwise equal-nnz slices per warp (on the power-law config
-  // 1.55x faster than ROWVEC_LX)
+  // lane group. Otherwise equal-nnz slices per warp: on the power-law config
+  // 2x faster than ROWVEC_LX, whose row kernel waits on each step's longest
+  // short row.
   if (mx <= 4.0 * avg + 32.0) {
     ch.variant = PF_VARIANT_ROWVEC;
     ch.lanes = rowvec_lanes(avg);

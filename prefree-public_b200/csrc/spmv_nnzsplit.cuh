@@ -72,8 +72,11 @@ struct LongRowScratch {
   int64_t cap_chunks;
 };
 
+// A row's chunks are the pieces of [s, e) in the aligned windows
+// [k * chunk, (k + 1) * chunk) of the absolute non-zero index, so that every
+// chunk lies in one window (the chunk kernel covers a window in one pass).
 __device__ __forceinline__ int64_t lx_num_chunks(int64_t s, int64_t e, int64_t chunk) {
-  return (e - s + chunk - 1) / chunk;
+  return e > s ? (e - 1) / chunk - s / chunk + 1 : 0;
 }
 
 // Descriptors of chunks [0, nch) of row `row` = [s, e), first chunk id `first`,
@@ -82,10 +85,11 @@ __device__ __forceinline__ void lx_write_chunks(const LongRowScratch &L, int64_t
                                                 int64_t e, int64_t first, int64_t chunk, int t,
                                                 int nthreads) {
   const int64_t nch = lx_num_chunks(s, e, chunk);
+  const int64_t w0 = s / chunk;
   for (int64_t c = t; c < nch; c += nthreads) {
-    const int64_t cs = s + c * chunk;
-    L.chunks[first + c] =
-        LongChunk{row, cs, first, (int32_t)min(chunk, e - cs), (int32_t)nch};
+    const int64_t cs = max(s, (w0 + c) * chunk);
+    const int64_t ce = min(e, (w0 + c + 1) * chunk);
+    L.chunks[first + c] = LongChunk{row, cs, first, (int32_t)(ce - cs), (int32_t)nch};
   }
 }
 

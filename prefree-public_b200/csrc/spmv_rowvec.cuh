@@ -322,14 +322,17 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
 }
 
 // Chunks of the listed long rows: warp w sums chunks w, w + W, ... (W warps in
-// the grid; the next descriptor is loaded while the current chunk is summed),
-// with 16-byte block loads, UNR blocks per lane in flight. A row of one chunk
-// is written at once; otherwise the chunk stores its partial and the last of
-// the row's chunks to finish sums the partials in chunk order (the same order
-// on every run) and writes y. The last CTA resets the counters.
-template <typename VT, typename IT, int NTB, int UNR = 2>
+// the grid; the next descriptor is loaded while the current chunk is summed).
+// A chunk lies in one aligned window of 128 * UNR non-zeros, which the warp
+// covers in one pass: every lane issues its UNR 16-byte column blocks, value
+// pieces and 4 * UNR x gathers at once. A row of one chunk is written at once;
+// otherwise the chunk stores its partial and the last of the row's chunks to
+// finish sums the partials in chunk order (the same order on every run) and
+// writes y. The last CTA resets the counters.
+template <typename VT, typename IT, int NTB, int UNR = 4>
 __global__ void __launch_bounds__(NTB)
 spmv_longrow_chunks_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L) {
+  constexpr int W = 128 * UNR;  // window = chunk length
   const int lane = threadIdx.x & 31;
   const int64_t n_chunks = (int64_t)*((volatile unsigned long long *)L.alloc);
   const int64_t warp = ((int64_t)blockIdx.x * NTB + threadIdx.x) >> 5;
@@ -341,26 +344,28 @@ spmv_longrow_chunks_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L) {
   for (int64_t g = warp; g < n_chunks; g += nwarps) {
     LongChunk nxt = cur;
     if (g + nwarps < n_chunks) nxt = L.chunks[g + nwarps];
-    const int64_t cs = cur.cs, ce = cur.cs + cur.len;
+    // offsets inside the chunk's window
+    const int64_t wb = cur.cs & ~(int64_t)(W - 1);
+    const int lo = (int)(cur.cs - wb), hi = lo + cur.len;
     double acc = 0.0;
-    for (int64_t q0 = (cs & ~(int64_t)3) + 4 * lane; q0 < ce; q0 += 4 * 32 * UNR) {
+    {
       int4 c4[UNR];
       VT v4[UNR][4];
 #pragma unroll
       for (int j = 0; j < UNR; ++j) {
-        const int64_t q = q0 + 4 * 32 * j;
-        const bool act = q < ce;
-        c4[j] = act ? __ldcs(reinterpret_cast<const int4 *>(P.col + q)) : make_int4(0, 0, 0, 0);
-        Block4<VT>::load(P.val, q, act && q + 1 >= cs, act && q + 2 < ce, v4[j]);
+        const int q = 4 * lane + 128 * j;
+        const bool act = q < hi && q + 4 > lo;
+        c4[j] = act ? __ldcs(reinterpret_cast<const int4 *>(P.col + wb + q)) : make_int4(0, 0, 0, 0);
+        Block4<VT>::load(P.val + wb, q, act && q + 1 >= lo, act && q + 2 < hi, v4[j]);
       }
       VT xv[UNR][4];
 #pragma unroll
       for (int j = 0; j < UNR; ++j) {
-        const int64_t q = q0 + 4 * 32 * j;
+        const int q = 4 * lane + 128 * j;
         const int cc[4] = {c4[j].x, c4[j].y, c4[j].z, c4[j].w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const bool use = q + i >= cs && q + i < ce;
+          const bool use = q + i >= lo && q + i < hi;
           const bool inb = (uint32_t)cc[i] < n;
           bad |= use && !inb;
           xv[j][i] = (use && inb) ? __ldg(P.x + cc[i]) : VT(0);
