@@ -203,11 +203,24 @@ def run_kernel_mode(args):
             spec = pf.GenSpec(cfg=cfg, seed=SEED, m=args.rows, n=args.cols).resolved()
             idt = torch.int64 if (cfg == 5 or args.int64) else torch.int32
             rp, col, val = pf.gen_rows_device(spec, index_dtype=idt, value_dtype=vdt)
-            x = pf.gen_x_device(spec, value_dtype=vdt)
-            y = torch.empty(spec.m, dtype=vdt, device="cuda")
             z = col.numel()
+            if args.k > 0:
+                # SpMM: k dense columns (x and its rotations), Y m x k
+                x0 = pf.gen_x_device(spec, value_dtype=vdt)
+                x = torch.stack([torch.roll(x0, j) for j in range(args.k)], dim=1).contiguous()
+                y = torch.empty(spec.m, args.k, dtype=vdt, device="cuda")
+                del x0
+
+                def one():
+                    pf.spmm(h, spec.m, spec.n, z, rp, col, val, x, y)
+            else:
+                x = pf.gen_x_device(spec, value_dtype=vdt)
+                y = torch.empty(spec.m, dtype=vdt, device="cuda")
+
+                def one():
+                    pf.spmv(h, spec.m, spec.n, z, rp, col, val, x, y)
             for _ in range(args.warmup):
-                pf.spmv(h, spec.m, spec.n, z, rp, col, val, x, y)
+                one()
             torch.cuda.synchronize()
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
@@ -218,7 +231,7 @@ def run_kernel_mode(args):
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g):
                     for _ in range(args.steps):
-                        pf.spmv(h, spec.m, spec.n, z, rp, col, val, x, y)
+                        one()
                 g.replay()
                 torch.cuda.synchronize()
                 e0.record()
@@ -227,15 +240,20 @@ def run_kernel_mode(args):
             else:
                 e0.record()
                 for _ in range(args.steps):
-                    pf.spmv(h, spec.m, spec.n, z, rp, col, val, x, y)
+                    one()
                 e1.record()
             torch.cuda.synchronize()
             assert h.device_error() == 0
             ms = e0.elapsed_time(e1) / args.steps
-            B = pf.compulsory_bytes(spec.m, spec.n, z, val.element_size(), rp.element_size())
+            kk = max(args.k, 1)
+            vs = val.element_size()
+            # compulsory bytes: A once, k columns of x and y
+            B = (pf.compulsory_bytes(spec.m, spec.n, z, vs, rp.element_size())
+                 + (kk - 1) * (spec.n + spec.m) * vs)
             print(json.dumps({"mode": "kernel", "config": cfg, "dtype": vname, "m": spec.m,
-                              "n": spec.n, "nnz": z, "variant": args.variant, "us": ms * 1e3,
-                              "gflops": 2 * z / ms / 1e6, "alg_GBps": B / ms / 1e6,
+                              "n": spec.n, "nnz": z, "variant": args.variant, "k": args.k,
+                              "us": ms * 1e3,
+                              "gflops": 2 * z * kk / ms / 1e6, "alg_GBps": B / ms / 1e6,
                               "frac_of_" + peak_src: B / ms / 1e6 / hbm_peak,
                               "frac_of_8TBps": B / ms / 1e6 / 8000.0,
                               "launches": args.steps, "graph": bool(args.graph)}), flush=True)
@@ -267,6 +285,8 @@ def main():
                     help="override m (kernel mode; power mode: profiling slice of config 5)")
     ap.add_argument("--cols", type=int, default=0, help="kernel mode: override n")
     ap.add_argument("--int64", action="store_true", help="kernel mode: int64 row_ptr")
+    ap.add_argument("--k", type=int, default=0,
+                    help="kernel mode: SpMM with k dense columns (0: SpMV)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="kernel mode: launch from Python instead of replaying a CUDA graph")
     args = ap.parse_args()

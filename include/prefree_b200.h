@@ -98,6 +98,31 @@ pf_status pf_spmv_f32_i64(pf_handle h, int64_t m, int64_t n, int64_t nnz,
                           const float *val, double alpha, const float *x,
                           double beta, float *y, void *stream);
 
+/* ---- SpMM: Y = alpha * A * X + beta * Y for k dense columns -----------------
+ * No counterpart in the reference (its harness multiplies one vector); the
+ * next step beside SpMV in iterative solvers with several right-hand sides.
+ * X is n x k and Y is m x k, both row-major on the device with leading
+ * dimensions ldx >= k and ldy >= k (elements). Columns are taken in passes
+ * of up to 8, each pass reading A once, so a non-zero's bytes and the cache
+ * line of its gather serve up to 8 products. Same CSR conventions, status
+ * codes and device error word as pf_spmv_*; asynchronous on `stream`.      */
+pf_status pf_spmm_f64_i32(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                          const int32_t *row_ptr, const int32_t *col_idx,
+                          const double *val, int k, double alpha, const double *X,
+                          int64_t ldx, double beta, double *Y, int64_t ldy, void *stream);
+pf_status pf_spmm_f64_i64(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                          const int64_t *row_ptr, const int32_t *col_idx,
+                          const double *val, int k, double alpha, const double *X,
+                          int64_t ldx, double beta, double *Y, int64_t ldy, void *stream);
+pf_status pf_spmm_f32_i32(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                          const int32_t *row_ptr, const int32_t *col_idx,
+                          const float *val, int k, double alpha, const float *X,
+                          int64_t ldx, double beta, float *Y, int64_t ldy, void *stream);
+pf_status pf_spmm_f32_i64(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                          const int64_t *row_ptr, const int32_t *col_idx,
+                          const float *val, int k, double alpha, const float *X,
+                          int64_t ldx, double beta, float *Y, int64_t ldy, void *stream);
+
 /* ---- fused multiply + all-gather for row-sharded iterated multiplies --------
  * No counterpart in the reference (single GPU only). One step of
  * x_{k+1} = A x_k / ||A x_k|| on this rank's row shard (rows

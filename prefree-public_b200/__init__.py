@@ -41,6 +41,7 @@ EXPORTED = [
     "pf_gen_resolve", "pf_gen_count", "pf_gen_row_lengths_host", "pf_gen_rows_host",
     "pf_gen_x_host", "pf_gen_rows_device", "pf_gen_x_device",
     "pf_spmv_noalloc_f64_i32", "pf_spmv_dist_f64_i64", "pf_spmv_dist_f64_i32",
+    "pf_spmm_f64_i32", "pf_spmm_f64_i64", "pf_spmm_f32_i32", "pf_spmm_f32_i64",
 ]
 # the C++ drop-in symbols of include/PreFree.h (mangled)
 CXX_EXPORTED = [
@@ -82,6 +83,10 @@ def _load():
                  "pf_spmv_host_f32_i64"):
         f = getattr(lib, name)
         f.argtypes = [vp, i64, i64, i64, vp, vp, vp, dbl, vp, dbl, vp, vp]
+        f.restype = st
+    for name in ("pf_spmm_f64_i32", "pf_spmm_f64_i64", "pf_spmm_f32_i32", "pf_spmm_f32_i64"):
+        f = getattr(lib, name)
+        f.argtypes = [vp, i64, i64, i64, vp, vp, vp, C.c_int, dbl, vp, i64, dbl, vp, i64, vp]
         f.restype = st
     for name in ("pf_spmv_dist_f64_i64", "pf_spmv_dist_f64_i32"):
         f = getattr(lib, name)
@@ -198,6 +203,23 @@ def spmv(handle: Handle, m: int, n: int, nnz: int, row_ptr, col, val, x, y,
     f = getattr(lib, "pf_spmv_" + _suffix(vsz, isz))
     _check(f(handle.ptr, int(m), int(n), int(nnz), _ptr(row_ptr), _ptr(col), _ptr(val),
              float(alpha), _ptr(x), float(beta), _ptr(y), C.c_void_p(stream)))
+
+
+def spmm(handle: Handle, m: int, n: int, nnz: int, row_ptr, col, val, X, Y,
+         alpha: float = 1.0, beta: float = 0.0, stream=None):
+    """Y = alpha*A*X + beta*Y for k = X.shape[1] dense columns (torch CUDA
+    tensors, X n x k and Y m x k, row-major with any row stride >= k)."""
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream().cuda_stream
+    elif hasattr(stream, "cuda_stream"):
+        stream = stream.cuda_stream
+    k = int(X.shape[1])
+    assert Y.shape[1] == k and X.stride(1) == 1 and Y.stride(1) == 1
+    f = getattr(lib, "pf_spmm_" + _suffix(val.element_size(), row_ptr.element_size()))
+    _check(f(handle.ptr, int(m), int(n), int(nnz), _ptr(row_ptr), _ptr(col), _ptr(val), k,
+             float(alpha), _ptr(X), int(X.stride(0)), float(beta), _ptr(Y), int(Y.stride(0)),
+             C.c_void_p(stream)))
 
 
 def spmv_dist(handle: Handle, m: int, n: int, nnz: int, row_ptr, col, val, x, prev_slots,

@@ -14,6 +14,7 @@
 #include "spmv_rowstream.cuh"
 #include "spmv_tma.cuh"
 #include "spmv_warpsplit.cuh"
+#include "spmm_rowvec.cuh"
 
 namespace pf {
 
@@ -653,6 +654,100 @@ pf_status prepare_matrix_i64(pf_handle h, int64_t m, int64_t nnz, const int64_t 
   return prepare_matrix<int64_t>(h, m, nnz, row_ptr, st);
 }
 
+// ---- SpMM: k dense columns, passes of up to 8 ------------------------------
+template <typename VT>
+__global__ void scale_block_kernel(int64_t m, int k, double beta, VT *__restrict__ Y, int64_t ldy) {
+  const int64_t total = m * (int64_t)k;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    VT *p = Y + (t / k) * ldy + (t % k);
+    *p = (beta != 0.0) ? (VT)(beta * (double)*p) : VT(0);
+  }
+}
+
+template <typename VT, typename IT, int V, int KC>
+static void launch_spmm_pass(pf_handle h, const SpmmParams<VT, IT> &p, bool vec, cudaStream_t st) {
+  constexpr int NTB = 256;
+  constexpr int XB = 16 / (int)sizeof(VT);  // X values per 16-byte piece
+  const int64_t rows_per_block = (int64_t)(NTB / 32) * (32 / V);
+  const int64_t grid = std::max<int64_t>(1, std::min(ceil_div(p.m, rows_per_block),
+                                                     (int64_t)h->num_sms * 16));
+  // 16-byte X loads: aligned rows, and the pass's pieces inside each row
+  const bool vx = KC >= XB && ((uintptr_t)p.X % 16) == 0 && p.ldx % XB == 0 &&
+                  ((p.kc + XB - 1) / XB) * XB <= p.ldx_left;
+  if (vec && vx) spmm_rowvec_kernel<VT, IT, V, KC, NTB, true, true><<<(unsigned)grid, NTB, 0, st>>>(p);
+  else if (vec) spmm_rowvec_kernel<VT, IT, V, KC, NTB, true, false><<<(unsigned)grid, NTB, 0, st>>>(p);
+  else spmm_rowvec_kernel<VT, IT, V, KC, NTB, false, false><<<(unsigned)grid, NTB, 0, st>>>(p);
+  count_launch();
+}
+
+template <typename VT, typename IT, int V>
+static void spmm_pass_kc(pf_handle h, const SpmmParams<VT, IT> &p, bool vec, cudaStream_t st) {
+  if (p.kc <= 1) launch_spmm_pass<VT, IT, V, 1>(h, p, vec, st);
+  else if (p.kc <= 2) launch_spmm_pass<VT, IT, V, 2>(h, p, vec, st);
+  else if (p.kc <= 4) launch_spmm_pass<VT, IT, V, 4>(h, p, vec, st);
+  else launch_spmm_pass<VT, IT, V, 8>(h, p, vec, st);
+}
+
+template <typename VT, typename IT>
+static pf_status launch_spmm(pf_handle h, int64_t m, int64_t n, int64_t nnz, const IT *row_ptr,
+                             const int32_t *col, const VT *val, int k, double alpha, const VT *X,
+                             int64_t ldx, double beta, VT *Y, int64_t ldy, cudaStream_t st) {
+  PF_CHECK_ARG(h != nullptr, "null handle");
+  PF_CHECK_ARG(m >= 0 && n >= 0 && nnz >= 0 && k >= 0, "negative size");
+  if (m == 0 || k == 0) return PF_OK;
+  PF_CHECK_ARG(row_ptr && Y, "null row_ptr or Y");
+  PF_CHECK_ARG(nnz == 0 || (col && val && X), "null col/val/X with nnz > 0");
+  PF_CHECK_ARG(ldy >= k && (nnz == 0 || ldx >= k), "leading dimension below k");
+  PF_CHECK_ARG(((uintptr_t)row_ptr % sizeof(IT)) == 0 && ((uintptr_t)Y % sizeof(VT)) == 0 &&
+                   (nnz == 0 || (((uintptr_t)col % 4) == 0 && ((uintptr_t)val % sizeof(VT)) == 0 &&
+                                 ((uintptr_t)X % sizeof(VT)) == 0)),
+               "arrays must be aligned to their element size");
+  int cur = 0;
+  PF_CUDA_TRY(cudaGetDevice(&cur));
+  PF_CHECK_ARG(cur == h->device, "handle bound to device %d, current device is %d",
+               h->device, cur);
+  if (nnz == 0) {
+    const int64_t blocks = std::min<int64_t>(ceil_div(m * (int64_t)k, (int64_t)256),
+                                             (int64_t)h->num_sms * 8);
+    scale_block_kernel<VT><<<(unsigned)blocks, 256, 0, st>>>(m, k, beta, Y, ldy);
+    count_launch();
+    PF_CUDA_TRY(cudaGetLastError());
+    return PF_OK;
+  }
+  // one contiguous column: the SpMV path (its variants and selector)
+  if (k == 1 && ldx == 1 && ldy == 1)
+    return launch_spmv<VT, IT>(h, m, n, nnz, row_ptr, col, val, alpha, X, beta, Y, st);
+  const bool vec = (((uintptr_t)col | (uintptr_t)val) & 15) == 0;
+  const int V = rowvec_lanes((double)nnz / (double)m);
+  for (int j0 = 0; j0 < k; j0 += 8) {
+    SpmmParams<VT, IT> p;
+    p.m = m;
+    p.n = n;
+    p.nnz = nnz;
+    p.row_ptr = row_ptr;
+    p.col = col;
+    p.val = val;
+    p.X = X + j0;
+    p.Y = Y + j0;
+    p.ldx = ldx;
+    p.ldy = ldy;
+    p.kc = std::min(8, k - j0);
+    p.ldx_left = ldx - j0;  // elements of an X row from this pass's first column
+    p.alpha = alpha;
+    p.beta = beta;
+    p.err = h->err;
+    switch (V) {
+      case 2: spmm_pass_kc<VT, IT, 2>(h, p, vec, st); break;
+      case 4: spmm_pass_kc<VT, IT, 4>(h, p, vec, st); break;
+      case 8: spmm_pass_kc<VT, IT, 8>(h, p, vec, st); break;
+      default: spmm_pass_kc<VT, IT, 16>(h, p, vec, st); break;
+    }
+    PF_CUDA_TRY(cudaGetLastError());
+  }
+  return PF_OK;
+}
+
 // Host-buffer call: copy in, one multiply, copy out.
 template <typename VT, typename IT>
 static pf_status host_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
@@ -796,6 +891,21 @@ pf_status pf_handle_device_error(pf_handle h, uint32_t *bits, int clear) {
     return host_spmv<VT, IT>(h, m, n, nnz, row_ptr, col_idx, val, alpha, x,    \
                              beta, y, (cudaStream_t)stream);                   \
   }
+
+#define PF_DEFINE_SPMM(SUFFIX, VT, IT)                                          \
+  pf_status pf_spmm_##SUFFIX(pf_handle h, int64_t m, int64_t n, int64_t nnz,   \
+                             const IT *row_ptr, const int32_t *col_idx,         \
+                             const VT *val, int k, double alpha, const VT *X,   \
+                             int64_t ldx, double beta, VT *Y, int64_t ldy,      \
+                             void *stream) {                                    \
+    return launch_spmm<VT, IT>(h, m, n, nnz, row_ptr, col_idx, val, k, alpha,  \
+                               X, ldx, beta, Y, ldy, (cudaStream_t)stream);    \
+  }
+
+PF_DEFINE_SPMM(f64_i32, double, int32_t)
+PF_DEFINE_SPMM(f64_i64, double, int64_t)
+PF_DEFINE_SPMM(f32_i32, float, int32_t)
+PF_DEFINE_SPMM(f32_i64, float, int64_t)
 
 pf_status pf_spmv_dist_f64_i64(pf_handle h, int64_t m, int64_t n, int64_t nnz,
                                const int64_t *row_ptr, const int32_t *col_idx,
