@@ -199,14 +199,17 @@ def run_kernel_mode(args):
     h.set_variant(args.variant)
     for cfg in [int(c) for c in args.config.split(",")]:
         for vname in args.dtype.split(","):
-            vdt = torch.float64 if vname == "f64" else torch.float32
+            vdt = {"f64": torch.float64, "f32": torch.float32, "f16": torch.float16,
+                   "bf16": torch.bfloat16}[vname]
+            gdt = vdt if vname in ("f64", "f32") else torch.float32  # generated, then rounded
             spec = pf.GenSpec(cfg=cfg, seed=SEED, m=args.rows, n=args.cols).resolved()
             idt = torch.int64 if (cfg == 5 or args.int64) else torch.int32
-            rp, col, val = pf.gen_rows_device(spec, index_dtype=idt, value_dtype=vdt)
+            rp, col, val = pf.gen_rows_device(spec, index_dtype=idt, value_dtype=gdt)
+            val = val.to(vdt)
             z = col.numel()
             if args.k > 0:
                 # SpMM: k dense columns (x and its rotations), Y m x k
-                x0 = pf.gen_x_device(spec, value_dtype=vdt)
+                x0 = pf.gen_x_device(spec, value_dtype=gdt).to(vdt)
                 x = torch.stack([torch.roll(x0, j) for j in range(args.k)], dim=1).contiguous()
                 y = torch.empty(spec.m, args.k, dtype=vdt, device="cuda")
                 del x0
@@ -214,7 +217,7 @@ def run_kernel_mode(args):
                 def one():
                     pf.spmm(h, spec.m, spec.n, z, rp, col, val, x, y)
             else:
-                x = pf.gen_x_device(spec, value_dtype=vdt)
+                x = pf.gen_x_device(spec, value_dtype=gdt).to(vdt)
                 y = torch.empty(spec.m, dtype=vdt, device="cuda")
 
                 def one():
@@ -279,7 +282,7 @@ def main():
                     help="power: the config-5 power iteration (the benchmark line); "
                          "kernel: per-config single-GPU multiply timing")
     ap.add_argument("--config", default="1,2,3,4,5", help="kernel mode: configs")
-    ap.add_argument("--dtype", default="f64", help="kernel mode: f64 and/or f32")
+    ap.add_argument("--dtype", default="f64", help="kernel mode: f64, f32, f16, bf16 (comma list)")
     ap.add_argument("--variant", type=int, default=0, help="kernel mode: 0 auto, 1-4 forced")
     ap.add_argument("--rows", type=int, default=0,
                     help="override m (kernel mode; power mode: profiling slice of config 5)")

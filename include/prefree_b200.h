@@ -98,6 +98,28 @@ pf_status pf_spmv_f32_i64(pf_handle h, int64_t m, int64_t n, int64_t nnz,
                           const float *val, double alpha, const float *x,
                           double beta, float *y, void *stream);
 
+/* ---- 16-bit values: binary16 (f16) and bfloat16 (bf16) ------------------------
+ * The reference's intended second value type (valT = half, include/common.h:
+ * 43-46; that build does not compile, src/spmv_kernel/preFreeSpMV.cu:326).
+ * val, x and y hold the 16-bit patterns; products and sums are computed in
+ * double and y is rounded once (to nearest). Otherwise as pf_spmv_*.        */
+pf_status pf_spmv_f16_i32(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                          const int32_t *row_ptr, const int32_t *col_idx,
+                          const uint16_t *val, double alpha, const uint16_t *x,
+                          double beta, uint16_t *y, void *stream);
+pf_status pf_spmv_f16_i64(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                          const int64_t *row_ptr, const int32_t *col_idx,
+                          const uint16_t *val, double alpha, const uint16_t *x,
+                          double beta, uint16_t *y, void *stream);
+pf_status pf_spmv_bf16_i32(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                           const int32_t *row_ptr, const int32_t *col_idx,
+                           const uint16_t *val, double alpha, const uint16_t *x,
+                           double beta, uint16_t *y, void *stream);
+pf_status pf_spmv_bf16_i64(pf_handle h, int64_t m, int64_t n, int64_t nnz,
+                           const int64_t *row_ptr, const int32_t *col_idx,
+                           const uint16_t *val, double alpha, const uint16_t *x,
+                           double beta, uint16_t *y, void *stream);
+
 /* ---- SpMM: Y = alpha * A * X + beta * Y for k dense columns -----------------
  * No counterpart in the reference (its harness multiplies one vector); the
  * next step beside SpMV in iterative solvers with several right-hand sides.

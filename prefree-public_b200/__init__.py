@@ -42,6 +42,7 @@ EXPORTED = [
     "pf_gen_x_host", "pf_gen_rows_device", "pf_gen_x_device",
     "pf_spmv_noalloc_f64_i32", "pf_spmv_dist_f64_i64", "pf_spmv_dist_f64_i32",
     "pf_spmm_f64_i32", "pf_spmm_f64_i64", "pf_spmm_f32_i32", "pf_spmm_f32_i64",
+    "pf_spmv_f16_i32", "pf_spmv_f16_i64", "pf_spmv_bf16_i32", "pf_spmv_bf16_i64",
 ]
 # the C++ drop-in symbols of include/PreFree.h (mangled)
 CXX_EXPORTED = [
@@ -79,6 +80,7 @@ def _load():
     lib.pf_handle_set_slice.argtypes = [vp, i64]
     lib.pf_handle_device_error.argtypes = [vp, C.POINTER(C.c_uint32), C.c_int]
     for name in ("pf_spmv_f64_i32", "pf_spmv_f64_i64", "pf_spmv_f32_i32", "pf_spmv_f32_i64",
+                 "pf_spmv_f16_i32", "pf_spmv_f16_i64", "pf_spmv_bf16_i32", "pf_spmv_bf16_i64",
                  "pf_spmv_host_f64_i32", "pf_spmv_host_f64_i64", "pf_spmv_host_f32_i32",
                  "pf_spmv_host_f32_i64"):
         f = getattr(lib, name)
@@ -182,8 +184,12 @@ class Handle:
             pass
 
 
-def _suffix(val_itemsize: int, idx_itemsize: int) -> str:
-    v = {8: "f64", 4: "f32"}[val_itemsize]
+def _suffix(val_itemsize: int, idx_itemsize: int, val_dtype=None) -> str:
+    if val_itemsize == 2:
+        import torch
+        v = "bf16" if val_dtype == torch.bfloat16 else "f16"
+    else:
+        v = {8: "f64", 4: "f32"}[val_itemsize]
     i = {4: "i32", 8: "i64"}[idx_itemsize]
     return f"{v}_{i}"
 
@@ -200,7 +206,7 @@ def spmv(handle: Handle, m: int, n: int, nnz: int, row_ptr, col, val, x, y,
         stream = stream.cuda_stream
     vsz = val.element_size() if hasattr(val, "element_size") else 8
     isz = row_ptr.element_size() if hasattr(row_ptr, "element_size") else 4
-    f = getattr(lib, "pf_spmv_" + _suffix(vsz, isz))
+    f = getattr(lib, "pf_spmv_" + _suffix(vsz, isz, getattr(val, "dtype", None)))
     _check(f(handle.ptr, int(m), int(n), int(nnz), _ptr(row_ptr), _ptr(col), _ptr(val),
              float(alpha), _ptr(x), float(beta), _ptr(y), C.c_void_p(stream)))
 

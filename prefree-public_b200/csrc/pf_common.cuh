@@ -2,6 +2,9 @@
 // bookkeeping and small device helpers shared by the kernels.
 #pragma once
 
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
 #include <cstdint>
 #include <cstdio>
 #include <cuda_runtime.h>
@@ -39,6 +42,18 @@ enum : unsigned {
 };
 
 // Count of our kernels launched since library load (bench reports it).
+// a 16-bit value from its bit pattern
+template <typename H>
+__device__ __forceinline__ H half_from_bits(unsigned short b);
+template <>
+__device__ __forceinline__ __half half_from_bits<__half>(unsigned short b) {
+  return __ushort_as_half(b);
+}
+template <>
+__device__ __forceinline__ __nv_bfloat16 half_from_bits<__nv_bfloat16>(unsigned short b) {
+  return __ushort_as_bfloat16(b);
+}
+
 extern unsigned long long g_launch_count;
 // spmv_api.cu: the one-time work of the first multiply with a matrix
 pf_status prepare_matrix_i32(pf_handle h, int64_t m, int64_t nnz, const int32_t *row_ptr,

@@ -6,6 +6,8 @@
 
 #include <cstdint>
 
+#include "pf_common.cuh"
+
 namespace pf {
 namespace ptx {
 
@@ -185,6 +187,25 @@ __device__ __forceinline__ int32_t ldg_hint<int32_t>(const int32_t *p, uint64_t 
   int32_t v;
   asm("ld.global.nc.L2::cache_hint.s32 %0, [%1], %2;" : "=r"(v) : "l"(p), "l"(policy));
   return v;
+}
+
+// 16-bit values: a 16-bit load of the bit pattern
+template <typename H>
+__device__ __forceinline__ H ldg_hint_16(const H *p, uint64_t policy) {
+  unsigned short v;
+  asm("ld.global.nc.L2::cache_hint.b16 %0, [%1], %2;" : "=h"(v) : "l"(p), "l"(policy));
+  return half_from_bits<H>(v);
+}
+
+template <>
+__device__ __forceinline__ __half ldg_hint<__half>(const __half *p, uint64_t policy) {
+  return ldg_hint_16(p, policy);
+}
+
+template <>
+__device__ __forceinline__ __nv_bfloat16 ldg_hint<__nv_bfloat16>(const __nv_bfloat16 *p,
+                                                                 uint64_t policy) {
+  return ldg_hint_16(p, policy);
 }
 
 }  // namespace ptx

@@ -476,6 +476,15 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
   pf_variant_choice ch;
   pf_status s = select_variant<IT>(h, m, nnz, row_ptr, st, &ch);
   if (s != PF_OK) return s;
+  constexpr bool kHalf = sizeof(VT) == 2;
+  if (kHalf) {
+    // 16-bit values run on the row-vector, warp-slice and plain-load kernels
+    const double avg = (double)nnz / (double)m;
+    if (ch.variant == PF_VARIANT_ROWSTREAM) ch = pf_variant_choice{PF_VARIANT_ROWVEC, rowvec_lanes(avg)};
+    if (ch.variant == PF_VARIANT_ROWSTREAM_LX)
+      ch = pf_variant_choice{PF_VARIANT_ROWVEC_LX, rowvec_lanes(avg)};
+    if (ch.variant == PF_VARIANT_NNZSPLIT) ch.variant = PF_VARIANT_NNZSPLIT_LDG;
+  }
 
   SpmvParams<VT, IT> prm;
   prm.m = m;
@@ -504,22 +513,24 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
     ch.variant = PF_VARIANT_ROWGROUP;
     ch.lanes = rowgroup_lanes(m > 0 ? (double)nnz / (double)m : 0.0);
   }
-  if (ch.variant == PF_VARIANT_ROWSTREAM || ch.variant == PF_VARIANT_ROWSTREAM_LX) {
-    // the long-row chunk kernel uses 16-byte loads: unaligned col/val keep
-    // long rows of unstaged tiles in the row kernel instead
-    const bool lx = ch.variant == PF_VARIANT_ROWSTREAM_LX &&
-                    (((uintptr_t)col | (uintptr_t)val) & 15) == 0;
-    prm.T = 0;
-    prm.num_ctas = 0;
-    prm.carry_head = prm.carry_tail = nullptr;
-    prm.counters = nullptr;
-    switch (ch.lanes) {
-      case 1: return launch_rowstream<VT, IT, 1>(h, prm, lx, st);
-      case 2: return launch_rowstream<VT, IT, 2>(h, prm, lx, st);
-      case 4: return launch_rowstream<VT, IT, 4>(h, prm, lx, st);
-      case 8: return launch_rowstream<VT, IT, 8>(h, prm, lx, st);
-      case 16: return launch_rowstream<VT, IT, 16>(h, prm, lx, st);
-      default: return launch_rowstream<VT, IT, 32>(h, prm, lx, st);
+  if constexpr (!kHalf) {
+    if (ch.variant == PF_VARIANT_ROWSTREAM || ch.variant == PF_VARIANT_ROWSTREAM_LX) {
+      // the long-row chunk kernel uses 16-byte loads: unaligned col/val keep
+      // long rows of unstaged tiles in the row kernel instead
+      const bool lx = ch.variant == PF_VARIANT_ROWSTREAM_LX &&
+                      (((uintptr_t)col | (uintptr_t)val) & 15) == 0;
+      prm.T = 0;
+      prm.num_ctas = 0;
+      prm.carry_head = prm.carry_tail = nullptr;
+      prm.counters = nullptr;
+      switch (ch.lanes) {
+        case 1: return launch_rowstream<VT, IT, 1>(h, prm, lx, st);
+        case 2: return launch_rowstream<VT, IT, 2>(h, prm, lx, st);
+        case 4: return launch_rowstream<VT, IT, 4>(h, prm, lx, st);
+        case 8: return launch_rowstream<VT, IT, 8>(h, prm, lx, st);
+        case 16: return launch_rowstream<VT, IT, 16>(h, prm, lx, st);
+        default: return launch_rowstream<VT, IT, 32>(h, prm, lx, st);
+      }
     }
   }
   if (ch.variant == PF_VARIANT_ROWVEC || ch.variant == PF_VARIANT_ROWVEC_LX) {
@@ -549,14 +560,17 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
     }
   }
 
-  const bool tma = (ch.variant == PF_VARIANT_NNZSPLIT);
+  const bool tma = !kHalf && (ch.variant == PF_VARIANT_NNZSPLIT);
   size_t smem = 0;
   int64_t T, min_T;
   int occ;
-  if (tma) {
-    occ = tma_occupancy<VT, IT>(&smem);
-    min_T = 2 * TmaCfgDefault::TILE;
-  } else {
+  if constexpr (!kHalf) {
+    if (tma) {
+      occ = tma_occupancy<VT, IT>(&smem);
+      min_T = 2 * TmaCfgDefault::TILE;
+    }
+  }
+  if (!tma) {
     occ = nnzsplit_occupancy<VT, IT>();
     min_T = NnzSplitCfg<VT, IT>::NT * NnzSplitCfg<VT, IT>::K;
   }
@@ -575,10 +589,13 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
   prm.carry_head = h->carry;
   prm.carry_tail = h->carry + h->cap;
   prm.counters = h->counters;
-  if (tma) {
-    using C = TmaCfgDefault;
-    spmv_tma_kernel<VT, IT, C><<<(unsigned)P, C::NT, smem, st>>>(prm);
-  } else {
+  if constexpr (!kHalf) {
+    if (tma) {
+      using C = TmaCfgDefault;
+      spmv_tma_kernel<VT, IT, C><<<(unsigned)P, C::NT, smem, st>>>(prm);
+    }
+  }
+  if (!tma) {
     using C = NnzSplitCfg<VT, IT>;
     spmv_nnzsplit_kernel<VT, IT, C::NT, C::K, C::W><<<(unsigned)P, C::NT, 0, st>>>(prm);
   }
@@ -891,6 +908,24 @@ pf_status pf_handle_device_error(pf_handle h, uint32_t *bits, int clear) {
     return host_spmv<VT, IT>(h, m, n, nnz, row_ptr, col_idx, val, alpha, x,    \
                              beta, y, (cudaStream_t)stream);                   \
   }
+
+// 16-bit values cross the C ABI as their raw bit patterns (uint16_t)
+#define PF_DEFINE_SPMV16(SUFFIX, VT, IT)                                        \
+  pf_status pf_spmv_##SUFFIX(pf_handle h, int64_t m, int64_t n, int64_t nnz,   \
+                             const IT *row_ptr, const int32_t *col_idx,         \
+                             const uint16_t *val, double alpha,                 \
+                             const uint16_t *x, double beta, uint16_t *y,       \
+                             void *stream) {                                    \
+    return launch_spmv<VT, IT>(h, m, n, nnz, row_ptr, col_idx,                 \
+                               reinterpret_cast<const VT *>(val), alpha,        \
+                               reinterpret_cast<const VT *>(x), beta,           \
+                               reinterpret_cast<VT *>(y), (cudaStream_t)stream); \
+  }
+
+PF_DEFINE_SPMV16(f16_i32, __half, int32_t)
+PF_DEFINE_SPMV16(f16_i64, __half, int64_t)
+PF_DEFINE_SPMV16(bf16_i32, __nv_bfloat16, int32_t)
+PF_DEFINE_SPMV16(bf16_i64, __nv_bfloat16, int64_t)
 
 #define PF_DEFINE_SPMM(SUFFIX, VT, IT)                                          \
   pf_status pf_spmm_##SUFFIX(pf_handle h, int64_t m, int64_t n, int64_t nnz,   \

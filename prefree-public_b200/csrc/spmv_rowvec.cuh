@@ -38,6 +38,25 @@ struct Block4<double> {
   }
 };
 
+// 16-bit values (binary16, bfloat16): the block's 4 values are one 8-byte piece
+template <typename H>
+struct Block4Half {
+  __device__ __forceinline__ static void load(const H *v, int64_t q, bool lo, bool hi, H out[4]) {
+    uint2 a = make_uint2(0u, 0u);
+    if (lo || hi) a = __ldcs(reinterpret_cast<const uint2 *>(v + q));
+    const uint32_t w[2] = {a.x, a.y};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const unsigned short bits = (unsigned short)(w[i >> 1] >> (16 * (i & 1)));
+      out[i] = half_from_bits<H>(bits);
+    }
+  }
+};
+template <>
+struct Block4<__half> : Block4Half<__half> {};
+template <>
+struct Block4<__nv_bfloat16> : Block4Half<__nv_bfloat16> {};
+
 template <>
 struct Block4<float> {
   __device__ __forceinline__ static void load(const float *v, int64_t q, bool lo, bool hi,

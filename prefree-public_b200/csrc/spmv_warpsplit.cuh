@@ -301,6 +301,15 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
             const double2 t = reinterpret_cast<const double2 *>(S.st[s].val + 8 * lane)[h];
             vv[0] = t.x;
             vv[1] = t.y;
+          } else if constexpr (VB == 8) {
+            // 16-bit values: the lane's 8 values are one 16-byte piece
+            const uint4 t = reinterpret_cast<const uint4 *>(S.st[s].val + 8 * lane)[h];
+            const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const unsigned short bits = (unsigned short)(w[i >> 1] >> (16 * (i & 1)));
+              vv[i] = half_from_bits<VT>(bits);
+            }
           } else {
             const float4 t = reinterpret_cast<const float4 *>(S.st[s].val + 8 * lane)[h];
             vv[0] = t.x;
