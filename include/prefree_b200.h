@@ -248,6 +248,24 @@ pf_status pf_mmio_read(const char *path, int64_t *m, int64_t *n, int64_t *nnz,
                        double **val);
 void pf_free(void *p);
 
+/* Binary CSR cache: parse a .mtx once, reload its CSR at file-read speed.
+ * pf_csr_write / pf_csr_read store and load (m, n, nnz, is_symmetric,
+ * row_ptr int64[m+1], col int32[nnz], val double[nnz]); pf_csr_read checks
+ * the file's size and the CSR's consistency (row_ptr non-decreasing from 0 to
+ * nnz, columns in [0, n)) before returning it. pf_mmio_read_cached reads
+ * cache_path when it was written from mtx_path's current size and
+ * modification time, else parses mtx_path with pf_mmio_read and (re)writes
+ * the cache, best effort. *from_cache (may be NULL) tells which happened.
+ * Arrays are malloc'd; free them with pf_free. No counterpart in the
+ * reference (its harness parses the text file on every run).                */
+pf_status pf_csr_write(const char *path, int64_t m, int64_t n, int64_t nnz, int is_symmetric,
+                       const int64_t *row_ptr, const int32_t *col_idx, const double *val);
+pf_status pf_csr_read(const char *path, int64_t *m, int64_t *n, int64_t *nnz, int *is_symmetric,
+                      int64_t **row_ptr, int32_t **col_idx, double **val);
+pf_status pf_mmio_read_cached(const char *mtx_path, const char *cache_path, int64_t *m,
+                              int64_t *n, int64_t *nnz, int *is_symmetric, int64_t **row_ptr,
+                              int32_t **col_idx, double **val, int *from_cache);
+
 /* ---- row sharding (multi-GPU) -----------------------------------------------
  * Equal-nnz row split: bounds[k] = first row r with row_ptr[r] - row_ptr[0]
  * >= k*nnz/parts (k = 0..parts; bounds[0] = 0, bounds[parts] = m). Host

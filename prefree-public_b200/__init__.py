@@ -43,6 +43,7 @@ EXPORTED = [
     "pf_spmv_noalloc_f64_i32", "pf_spmv_dist_f64_i64", "pf_spmv_dist_f64_i32",
     "pf_spmm_f64_i32", "pf_spmm_f64_i64", "pf_spmm_f32_i32", "pf_spmm_f32_i64",
     "pf_spmv_f16_i32", "pf_spmv_f16_i64", "pf_spmv_bf16_i32", "pf_spmv_bf16_i64",
+    "pf_csr_write", "pf_csr_read", "pf_mmio_read_cached",
 ]
 # the C++ drop-in symbols of include/PreFree.h (mangled)
 CXX_EXPORTED = [
@@ -104,6 +105,11 @@ def _load():
     lib.pf_mmio_read.argtypes = [C.c_char_p, C.POINTER(i64), C.POINTER(i64), C.POINTER(i64),
                                  C.POINTER(C.c_int), C.POINTER(vp), C.POINTER(vp),
                                  C.POINTER(vp)]
+    csr_out = [C.POINTER(i64), C.POINTER(i64), C.POINTER(i64), C.POINTER(C.c_int),
+               C.POINTER(vp), C.POINTER(vp), C.POINTER(vp)]
+    lib.pf_csr_write.argtypes = [C.c_char_p, i64, i64, i64, C.c_int, vp, vp, vp]
+    lib.pf_csr_read.argtypes = [C.c_char_p] + csr_out
+    lib.pf_mmio_read_cached.argtypes = [C.c_char_p, C.c_char_p] + csr_out + [C.POINTER(C.c_int)]
     lib.pf_free.argtypes = [vp]
     lib.pf_free.restype = None
     lib.pf_shard_bounds_i32.argtypes = [vp, i64, C.c_int, vp]
@@ -278,13 +284,7 @@ def preFreeSpMV(csrVal: np.ndarray, csrRowPtr: np.ndarray, csrColInd: np.ndarray
 # ---------------------------------------------------------------------------
 # Matrix Market input path and sharding
 # ---------------------------------------------------------------------------
-def mmio_read(path: str):
-    """Matrix Market -> CSR (mmio_allinone semantics). Returns
-    (m, n, nnz, is_symmetric, row_ptr int64[m+1], col int32[nnz], val f64[nnz])."""
-    m, n, z, sym = C.c_int64(), C.c_int64(), C.c_int64(), C.c_int()
-    rp, ci, va = C.c_void_p(), C.c_void_p(), C.c_void_p()
-    _check(lib.pf_mmio_read(os.fsencode(path), C.byref(m), C.byref(n), C.byref(z),
-                            C.byref(sym), C.byref(rp), C.byref(ci), C.byref(va)))
+def _take_csr(m, n, z, sym, rp, ci, va):
     try:
         row_ptr = np.ctypeslib.as_array(C.cast(rp, C.POINTER(C.c_int64)), (m.value + 1,)).copy()
         col = np.ctypeslib.as_array(C.cast(ci, C.POINTER(C.c_int32)), (max(z.value, 1),))[
@@ -296,6 +296,44 @@ def mmio_read(path: str):
         lib.pf_free(ci)
         lib.pf_free(va)
     return m.value, n.value, z.value, bool(sym.value), row_ptr, col, val
+
+
+def _csr_out():
+    return (C.c_int64(), C.c_int64(), C.c_int64(), C.c_int(), C.c_void_p(), C.c_void_p(),
+            C.c_void_p())
+
+
+def mmio_read(path: str):
+    """Matrix Market -> CSR (mmio_allinone semantics). Returns
+    (m, n, nnz, is_symmetric, row_ptr int64[m+1], col int32[nnz], val f64[nnz])."""
+    o = _csr_out()
+    _check(lib.pf_mmio_read(os.fsencode(path), *[C.byref(v) for v in o]))
+    return _take_csr(*o)
+
+
+def csr_write(path: str, m: int, n: int, row_ptr, col, val, is_symmetric: bool = False):
+    """Store a CSR (int64 row_ptr, int32 col, f64 val) in the binary cache format."""
+    rp = np.ascontiguousarray(row_ptr, dtype=np.int64)
+    ci = np.ascontiguousarray(col, dtype=np.int32)
+    va = np.ascontiguousarray(val, dtype=np.float64)
+    _check(lib.pf_csr_write(os.fsencode(path), int(m), int(n), len(ci), int(is_symmetric),
+                            rp.ctypes.data, ci.ctypes.data, va.ctypes.data))
+
+
+def csr_read(path: str):
+    """Load a binary CSR cache file; same return value as mmio_read."""
+    o = _csr_out()
+    _check(lib.pf_csr_read(os.fsencode(path), *[C.byref(v) for v in o]))
+    return _take_csr(*o)
+
+
+def mmio_read_cached(mtx_path: str, cache_path: str):
+    """mmio_read through a binary cache: returns (csr tuple, from_cache)."""
+    o = _csr_out()
+    fc = C.c_int()
+    _check(lib.pf_mmio_read_cached(os.fsencode(mtx_path), os.fsencode(cache_path),
+                                   *[C.byref(v) for v in o], C.byref(fc)))
+    return _take_csr(*o), bool(fc.value)
 
 
 def shard_bounds(row_ptr: np.ndarray, parts: int) -> np.ndarray:

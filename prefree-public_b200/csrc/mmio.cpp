@@ -29,6 +29,8 @@
 #include <thread>
 #include <vector>
 
+#include <sys/stat.h>
+
 #include "../../include/prefree_b200.h"
 
 namespace pf {
@@ -327,6 +329,151 @@ pf_status pf_mmio_read(const char *path, int64_t *m_out, int64_t *n_out,
   *row_ptr_out = rp;
   *col_out = col;
   *val_out = val;
+  return PF_OK;
+}
+
+// ---- binary CSR cache ---------------------------------------------------------
+// File: a 64-byte header {magic "PFCSR001", m, n, nnz, is_symmetric, source
+// size, source mtime in ns, 0}, then row_ptr (int64, m+1), col (int32, nnz),
+// val (double, nnz), all little-endian as in memory.
+
+struct CsrHeader {
+  char magic[8];
+  int64_t m, n, nnz, sym, src_size, src_mtime_ns, pad;
+};
+static const char kCsrMagic[8] = {'P', 'F', 'C', 'S', 'R', '0', '0', '1'};
+
+static bool file_stamp(const char *path, int64_t *size, int64_t *mtime_ns) {
+  struct stat st;
+  if (stat(path, &st) != 0) return false;
+  *size = (int64_t)st.st_size;
+  *mtime_ns = (int64_t)st.st_mtim.tv_sec * 1000000000LL + (int64_t)st.st_mtim.tv_nsec;
+  return true;
+}
+
+static pf_status csr_write(const char *path, int64_t m, int64_t n, int64_t nnz, int sym,
+                           const int64_t *rp, const int32_t *col, const double *val,
+                           int64_t src_size, int64_t src_mtime_ns) {
+  if (!path || m < 0 || n < 0 || nnz < 0 || !rp || (nnz > 0 && (!col || !val))) {
+    pf::set_error("pf_csr_write: bad argument");
+    return PF_ERR_INVALID;
+  }
+  const std::string tmp = std::string(path) + ".tmp";
+  FILE *f = std::fopen(tmp.c_str(), "wb");
+  if (!f) {
+    pf::set_error("pf_csr_write: cannot create %s: %s", tmp.c_str(), std::strerror(errno));
+    return PF_ERR_IO;
+  }
+  CsrHeader hd;
+  std::memcpy(hd.magic, kCsrMagic, 8);
+  hd.m = m;
+  hd.n = n;
+  hd.nnz = nnz;
+  hd.sym = sym;
+  hd.src_size = src_size;
+  hd.src_mtime_ns = src_mtime_ns;
+  hd.pad = 0;
+  bool ok = std::fwrite(&hd, sizeof(hd), 1, f) == 1 &&
+            std::fwrite(rp, sizeof(int64_t), (size_t)m + 1, f) == (size_t)m + 1 &&
+            (nnz == 0 || (std::fwrite(col, sizeof(int32_t), (size_t)nnz, f) == (size_t)nnz &&
+                          std::fwrite(val, sizeof(double), (size_t)nnz, f) == (size_t)nnz));
+  ok = (std::fclose(f) == 0) && ok;
+  if (!ok || std::rename(tmp.c_str(), path) != 0) {
+    std::remove(tmp.c_str());
+    pf::set_error("pf_csr_write: write to %s failed", path);
+    return PF_ERR_IO;
+  }
+  return PF_OK;
+}
+
+// Reads a cache file; with want_size >= 0 the recorded source stamp must
+// match (want_size, want_mtime), else PF_ERR_FORMAT.
+static pf_status csr_read(const char *path, int64_t want_size, int64_t want_mtime, int64_t *m_out,
+                          int64_t *n_out, int64_t *nnz_out, int *sym_out, int64_t **rp_out,
+                          int32_t **col_out, double **val_out) {
+  FILE *f = std::fopen(path, "rb");
+  if (!f) {
+    pf::set_error("pf_csr_read: cannot open %s: %s", path, std::strerror(errno));
+    return PF_ERR_IO;
+  }
+  CsrHeader hd;
+  int64_t fsize = -1, fmt = 0;
+  file_stamp(path, &fsize, &fmt);
+  if (std::fread(&hd, sizeof(hd), 1, f) != 1 || std::memcmp(hd.magic, kCsrMagic, 8) != 0 ||
+      hd.m < 0 || hd.n < 0 || hd.nnz < 0 || hd.m >= ((int64_t)1 << 40) ||
+      hd.nnz >= ((int64_t)1 << 40) ||
+      fsize != (int64_t)sizeof(hd) + 8 * (hd.m + 1) + 12 * hd.nnz ||
+      (want_size >= 0 && (hd.src_size != want_size || hd.src_mtime_ns != want_mtime))) {
+    std::fclose(f);
+    pf::set_error("pf_csr_read: %s is not a matching CSR cache file", path);
+    return PF_ERR_FORMAT;
+  }
+  int64_t *rp = (int64_t *)std::malloc(sizeof(int64_t) * (size_t)(hd.m + 1));
+  int32_t *col = (int32_t *)std::malloc(sizeof(int32_t) * (size_t)std::max<int64_t>(hd.nnz, 1));
+  double *val = (double *)std::malloc(sizeof(double) * (size_t)std::max<int64_t>(hd.nnz, 1));
+  bool ok = rp && col && val &&
+            std::fread(rp, sizeof(int64_t), (size_t)hd.m + 1, f) == (size_t)hd.m + 1 &&
+            (hd.nnz == 0 ||
+             (std::fread(col, sizeof(int32_t), (size_t)hd.nnz, f) == (size_t)hd.nnz &&
+              std::fread(val, sizeof(double), (size_t)hd.nnz, f) == (size_t)hd.nnz));
+  std::fclose(f);
+  // the CSR must be consistent before anyone indexes with it
+  if (ok) ok = rp[0] == 0 && rp[hd.m] == hd.nnz;
+  for (int64_t r = 0; ok && r < hd.m; ++r) ok = rp[r] <= rp[r + 1];
+  for (int64_t k = 0; ok && k < hd.nnz; ++k) ok = col[k] >= 0 && (int64_t)col[k] < hd.n;
+  if (!ok) {
+    std::free(rp);
+    std::free(col);
+    std::free(val);
+    pf::set_error("pf_csr_read: %s is truncated or inconsistent", path);
+    return PF_ERR_FORMAT;
+  }
+  *m_out = hd.m;
+  *n_out = hd.n;
+  *nnz_out = hd.nnz;
+  *sym_out = (int)hd.sym;
+  *rp_out = rp;
+  *col_out = col;
+  *val_out = val;
+  return PF_OK;
+}
+
+pf_status pf_csr_write(const char *path, int64_t m, int64_t n, int64_t nnz, int is_symmetric,
+                       const int64_t *row_ptr, const int32_t *col_idx, const double *val) {
+  return csr_write(path, m, n, nnz, is_symmetric, row_ptr, col_idx, val, -1, 0);
+}
+
+pf_status pf_csr_read(const char *path, int64_t *m, int64_t *n, int64_t *nnz, int *is_symmetric,
+                      int64_t **row_ptr, int32_t **col_idx, double **val) {
+  if (!path || !m || !n || !nnz || !is_symmetric || !row_ptr || !col_idx || !val) {
+    pf::set_error("pf_csr_read: null argument");
+    return PF_ERR_INVALID;
+  }
+  return csr_read(path, -1, 0, m, n, nnz, is_symmetric, row_ptr, col_idx, val);
+}
+
+pf_status pf_mmio_read_cached(const char *mtx_path, const char *cache_path, int64_t *m,
+                              int64_t *n, int64_t *nnz, int *is_symmetric, int64_t **row_ptr,
+                              int32_t **col_idx, double **val, int *from_cache) {
+  if (!mtx_path || !cache_path || !m || !n || !nnz || !is_symmetric || !row_ptr || !col_idx ||
+      !val) {
+    pf::set_error("pf_mmio_read_cached: null argument");
+    return PF_ERR_INVALID;
+  }
+  int64_t sz = 0, mt = 0;
+  if (!file_stamp(mtx_path, &sz, &mt)) {
+    pf::set_error("pf_mmio_read_cached: cannot stat %s: %s", mtx_path, std::strerror(errno));
+    return PF_ERR_IO;
+  }
+  if (from_cache) *from_cache = 0;
+  if (csr_read(cache_path, sz, mt, m, n, nnz, is_symmetric, row_ptr, col_idx, val) == PF_OK) {
+    if (from_cache) *from_cache = 1;
+    return PF_OK;
+  }
+  pf_status st = pf_mmio_read(mtx_path, m, n, nnz, is_symmetric, row_ptr, col_idx, val);
+  if (st != PF_OK) return st;
+  // best effort: a cache that cannot be written only costs the next parse
+  csr_write(cache_path, *m, *n, *nnz, *is_symmetric, *row_ptr, *col_idx, *val, sz, mt);
   return PF_OK;
 }
 
