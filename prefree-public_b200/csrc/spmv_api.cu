@@ -617,9 +617,12 @@ static pf_status launch_warpsplit(pf_handle h, SpmvParams<VT, IT> prm, cudaStrea
 #ifndef PF_WS_MINB
 #define PF_WS_MINB 3
 #endif
-  constexpr int NTB = 256, WIN = PF_WS_WIN, NS = PF_WS_NS, MINB = PF_WS_MINB;
-  auto kern = spmv_warpsplit_kernel<VT, IT, NTB, WIN, NS, MINB>;
-  const size_t smem = sizeof(WarpSplitSmem<VT, WIN, NS>) * (NTB / 32);
+#ifndef PF_WS_EPL
+#define PF_WS_EPL 8
+#endif
+  constexpr int NTB = 256, WIN = PF_WS_WIN, NS = PF_WS_NS, MINB = PF_WS_MINB, EPL = PF_WS_EPL;
+  auto kern = spmv_warpsplit_kernel<VT, IT, NTB, WIN, NS, MINB, EPL>;
+  const size_t smem = sizeof(WarpSplitSmem<VT, WIN, NS, EPL>) * (NTB / 32);
   static int occ = -1;
   if (occ < 0) {
     PF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -629,7 +632,7 @@ static pf_status launch_warpsplit(pf_handle h, SpmvParams<VT, IT> prm, cudaStrea
   }
   const int64_t warps = (int64_t)h->num_sms * occ * (NTB / 32);
   const int64_t T = h->slice_override > 0 ? h->slice_override
-                                          : std::max<int64_t>(ceil_div(prm.nnz, warps), 256);
+                                          : std::max<int64_t>(ceil_div(prm.nnz, warps), 32 * EPL);
   const int64_t P = ceil_div(prm.nnz, T);
   PF_CHECK_ARG(P <= INT32_MAX, "too many slices");
   PF_CHECK_ARG(T < INT32_MAX, "slice too long");

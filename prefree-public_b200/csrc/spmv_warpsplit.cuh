@@ -2,7 +2,7 @@
 //
 // The non-zeros [base, base + nnz) are cut into slices of T; warp w takes
 // slices w, w + W, ... (W warps in the grid). A warp walks its slice in tiles
-// of 256 non-zeros aligned to absolute multiples of 256. Lane 0 streams the
+// of 32 * EPL non-zeros aligned to absolute multiples of that. Lane 0 streams the
 // tiles' columns and values into the warp's own ring of NS shared-memory
 // stages with bulk copies (cp.async.bulk, completion on one mbarrier per
 // stage, every wait bounded), NS tiles ahead of the tile being summed, so the
@@ -51,11 +51,11 @@ __device__ __forceinline__ int window_upper_bound(const int *E, int key) {
   return (E[lo] <= key) ? lo + 1 : lo;
 }
 
-template <typename VT, int WIN, int NS>
+template <typename VT, int WIN, int NS, int EPL = 8>
 struct WarpSplitSmem {
   struct Stage {
-    alignas(128) int32_t col[256];
-    alignas(128) VT val[256];
+    alignas(128) int32_t col[32 * EPL];
+    alignas(128) VT val[32 * EPL];
   };
   Stage st[NS];
   int win[WIN];
@@ -65,14 +65,14 @@ struct WarpSplitSmem {
 // Positions inside a slice are 32-bit offsets from its first non-zero S0
 // (a slice holds fewer than 2^31 non-zeros); the window holds row ends as
 // such offsets, INT_MAX for rows that never end in this slice.
-template <typename VT, typename IT, int NTB, int WIN, int NS, int MINB>
+template <typename VT, typename IT, int NTB, int WIN, int NS, int MINB, int EPL = 8>
 __global__ void __launch_bounds__(NTB, MINB)
 spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
   constexpr int NW = NTB / 32;
-  constexpr int TILE = 256;  // 32 lanes x 8 non-zeros
+  constexpr int TILE = 32 * EPL;  // 32 lanes x EPL non-zeros
   constexpr int NEVER = INT32_MAX;
   constexpr int VB = 16 / (int)sizeof(VT);  // values per 16-byte block
-  using Smem = WarpSplitSmem<VT, WIN, NS>;
+  using Smem = WarpSplitSmem<VT, WIN, NS, EPL>;
   extern __shared__ __align__(128) unsigned char ws_raw[];
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
@@ -177,16 +177,16 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
     // lie in [g, te] (the lane holding g takes the ends at g) and carries the
     // rest. MASK: the pass covers only part of the tile's non-zeros. False if
     // nothing moved (only a decreasing row_ptr).
-    auto pass = [&](int tb, int te, const double(&p)[8], bool mask) -> bool {
-      const int lo = tb + 8 * lane;
-      const int a = min(max(lo, g), te), b = min(max(lo + 8, g), te);
-      const bool owner = ((g - tb) >> 3) == lane;
+    auto pass = [&](int tb, int te, const double(&p)[EPL], bool mask) -> bool {
+      const int lo = tb + EPL * lane;
+      const int a = min(max(lo, g), te), b = min(max(lo + EPL, g), te);
+      const bool owner = (g - tb) / EPL == lane;
       int jj = owner ? off : window_upper_bound<WIN>(E, a);
       int nend = jj < WIN ? E[jj] : NEVER;  // next row end
       double acc = 0.0, head = 0.0;
       int first_j = -1;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < EPL; ++i) {
         const int pos = lo + i;
         if (pos >= a && pos < b) {
           if (nend <= pos) {
@@ -265,16 +265,22 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
     // x gathers of tile i (columns from its stage), issued a tile ahead of
     // its sum so that they are in flight while the previous tile is walked
     const int tb0 = (int)(T0 - S0);  // first tile base, relative (> -256)
-    VT xv[8];
+    VT xv[EPL];
     auto gather = [&](int i) {
-      const int tb = tb0 + i * TILE, lo = tb + 8 * lane;
+      const int tb = tb0 + i * TILE, lo = tb + EPL * lane;
       const int ga = max(tb, 0), gb = min(tb + TILE, L);
-      const int32_t *cs = S.st[(kk + (uint32_t)i) % NS].col + 8 * lane;
-      const int4 c0 = *reinterpret_cast<const int4 *>(cs);
-      const int4 c1 = *reinterpret_cast<const int4 *>(cs + 4);
-      const int cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const int32_t *cs = S.st[(kk + (uint32_t)i) % NS].col + EPL * lane;
+      int cc[EPL];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
+      for (int b = 0; b < EPL / 4; ++b) {
+        const int4 c4 = reinterpret_cast<const int4 *>(cs)[b];
+        cc[4 * b] = c4.x;
+        cc[4 * b + 1] = c4.y;
+        cc[4 * b + 2] = c4.z;
+        cc[4 * b + 3] = c4.w;
+      }
+#pragma unroll
+      for (int q = 0; q < EPL; ++q) {
         const bool use = lo + q >= ga && lo + q < gb;
         const bool inb = (uint32_t)cc[q] < n;
         bad |= use && !inb;
@@ -289,21 +295,21 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
       const int s = (int)((kk + (uint32_t)i) % NS);
       const int tb = tb0 + i * TILE;
       const int tend = min(tb + TILE, L);
-      const int lo = tb + 8 * lane;
+      const int lo = tb + EPL * lane;
       // products of tile i (x gathered during the previous tile)
-      double p[8];
+      double p[EPL];
       {
         const int ga = max(tb, 0);
 #pragma unroll
-        for (int h = 0; h < 8 / VB; ++h) {
+        for (int h = 0; h < EPL / VB; ++h) {
           VT vv[VB];
           if constexpr (VB == 2) {
-            const double2 t = reinterpret_cast<const double2 *>(S.st[s].val + 8 * lane)[h];
+            const double2 t = reinterpret_cast<const double2 *>(S.st[s].val + EPL * lane)[h];
             vv[0] = t.x;
             vv[1] = t.y;
           } else if constexpr (VB == 8) {
-            // 16-bit values: the lane's 8 values are one 16-byte piece
-            const uint4 t = reinterpret_cast<const uint4 *>(S.st[s].val + 8 * lane)[h];
+            // 16-bit values: 8 values per 16-byte piece
+            const uint4 t = reinterpret_cast<const uint4 *>(S.st[s].val + EPL * lane)[h];
             const uint32_t w[4] = {t.x, t.y, t.z, t.w};
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
@@ -311,7 +317,7 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
               vv[i] = half_from_bits<VT>(bits);
             }
           } else {
-            const float4 t = reinterpret_cast<const float4 *>(S.st[s].val + 8 * lane)[h];
+            const float4 t = reinterpret_cast<const float4 *>(S.st[s].val + EPL * lane)[h];
             vv[0] = t.x;
             vv[1] = t.y;
             vv[2] = t.z;
@@ -339,7 +345,10 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
       if (off >= WIN / 2) load_window();
       if (E[off] > tend) {
         // no row ends in this tile: a plain sum into the current row
-        double t = ((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7]));
+        double t = 0.0;
+#pragma unroll
+        for (int q = 0; q < EPL; q += 8)
+          t += ((p[q] + p[q + 1]) + (p[q + 2] + p[q + 3])) + ((p[q + 4] + p[q + 5]) + (p[q + 6] + p[q + 7]));
 #pragma unroll
         for (int d = 16; d > 0; d >>= 1) t += __shfl_xor_sync(0xffffffffu, t, d);
         carry += t;
@@ -367,7 +376,9 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
         if (lane == 0) contribute_cut_row(P, base, rw + off, rw + off == head_row, c, carry);
         break;
       }
-      const double z[8] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0};
+      double z[EPL];
+#pragma unroll
+      for (int q = 0; q < EPL; ++q) z[q] = 0.0;
       ok = pass((int)((S1 & ~(int64_t)(TILE - 1)) - S0), L, z, false);
     }
     if (!ok && lane == 0) atomicOr(P.err, PF_DEVERR_ROWPTR);
