@@ -7,7 +7,7 @@ Workload (the largest config; it fits one GPU):
 data (counter-based generator, seed 12345). One step = one iterated multiply
 y <- A*y/||y|| over equal-nnz row shards: by default one fused kernel per rank
 (rows stored straight into every rank's next x over NVLink, ||y||^2 reduced
-in the kernel, alpha = 1/||x|| read on the device) and a cross-rank barrier;
+in the kernel, alpha = 1/||x|| read on the device, the cross-rank step barrier in the kernel);
 `--path nccl` runs the local SpMV + NCCL all-reduce/all-gather instead.
 `scaling` is "strong": the matrix is fixed, N GPUs share it.
 
@@ -348,7 +348,9 @@ def main():
 
     if args.path == "fused":
         # one kernel per step: rows go straight into every rank's next x over
-        # NVLink, ||y||^2 is reduced in the kernel, then a cross-rank barrier
+        # NVLink, ||y||^2 is reduced in the kernel, and the kernel waits for
+        # every rank's previous step (step counters) before reading x: steps
+        # are launched back to back
         fused = pfd.FusedPowerIteration(pf, h, rp, col, val, x, bounds, rank, world,
                                         stream=stream)
 
@@ -357,15 +359,14 @@ def main():
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
+                fp = fused.flag_ptrs.data_ptr() if fused.flag_ptrs is not None else 0
                 pf.spmv_dist(h, m_loc, n, nnz_loc, rp, col, val, fused.xs[fused.k % 2],
                              fused.slots[fused.k % 2], world, rank,
                              fused.out_ptrs[(fused.k + 1) % 2].data_ptr(),
                              fused.slot_ptrs[(fused.k + 1) % 2].data_ptr(), int(bounds[rank]),
-                             stream=stream)
+                             stream=stream, flag_ptrs_dev=fp, step=fused.k)
                 e1.record(stream)
                 ev_pairs.append((e0, e1))
-                if fused.hdl is not None:
-                    fused.hdl.barrier(channel=0)
                 fused.k += 1
                 return None
         it = _Step()
@@ -485,7 +486,7 @@ def main():
             "config": {"workload": WORKLOAD, "m": spec.m, "n": spec.n, "nnz": z_tot,
                        "index": "int64 row_ptr, int32 col", "parallelism": f"row shards x{world}",
                        "l2": "inputs (27 GB) larger than L2: no flush",
-                       "step": ("fused: SpMV storing rows into every rank's next x over NVLink + in-kernel ||y||^2 + cross-rank barrier"
+                       "step": ("fused: SpMV storing rows into every rank's next x over NVLink + in-kernel ||y||^2 + in-kernel cross-rank step barrier"
                                 if args.path == "fused" else
                                 "local SpMV + NCCL all-reduce ||y||^2 + NCCL all-gather y")},
             "gpu_launches": int(launches),

@@ -155,20 +155,30 @@ pf_status pf_spmm_f32_i64(pf_handle h, int64_t m, int64_t n, int64_t nnz,
  *   pointers: each rank's next-x buffer, peers' reachable over NVLink);
  *   ||y||^2 of this rank's rows is reduced in the same kernel (fixed order:
  *   the same bits every run) and stored to slot_ptrs[p][rank] for every p.
- * The caller puts a cross-rank barrier between steps (peers' stores must
- * land before the next step reads x, and nobody may overwrite a buffer a
- * peer still reads: alternate two x buffers and two slot arrays). fp64 values,
- * col/val 16-byte aligned (ROWVEC kernel). Asynchronous on `stream`.        */
+ * Steps must be separated by a cross-rank barrier (peers' stores must land
+ * before the next step reads x, and nobody may overwrite a buffer a peer
+ * still reads: alternate two x buffers and two slot arrays). With flag_ptrs
+ * (device array of nranks pointers to every rank's array of nranks uint64
+ * step counters, zero at the start, peer-mapped like out_ptrs) the kernel
+ * is that barrier: step `step` (0, 1, ...) waits, one thread per CTA, until
+ * its own counters all reach `step`, and when its stores are done it sets
+ * counter `rank` to step + 1 on every rank; the host then launches steps
+ * back to back. The wait gives up after 1 s with PF_DEVERR_WAIT_TIMEOUT in
+ * the device error word. flag_ptrs = NULL: no barrier in the kernel (the
+ * caller provides one). fp64 values, col/val 16-byte aligned (ROWVEC
+ * kernel). Asynchronous on `stream`.                                        */
 pf_status pf_spmv_dist_f64_i64(pf_handle h, int64_t m, int64_t n, int64_t nnz,
                                const int64_t *row_ptr, const int32_t *col_idx,
                                const double *val, const double *x, const double *prev_slots,
                                int nranks, int rank, double *const *out_ptrs,
-                               double *const *slot_ptrs, int64_t row_offset, void *stream);
+                               double *const *slot_ptrs, int64_t row_offset,
+                               uint64_t *const *flag_ptrs, uint64_t step, void *stream);
 pf_status pf_spmv_dist_f64_i32(pf_handle h, int64_t m, int64_t n, int64_t nnz,
                                const int32_t *row_ptr, const int32_t *col_idx,
                                const double *val, const double *x, const double *prev_slots,
                                int nranks, int rank, double *const *out_ptrs,
-                               double *const *slot_ptrs, int64_t row_offset, void *stream);
+                               double *const *slot_ptrs, int64_t row_offset,
+                               uint64_t *const *flag_ptrs, uint64_t step, void *stream);
 
 /* ---- allocation-free multiply (fp64 values, int32 row_ptr) ------------------
  * No counterpart in the reference. For callers that cannot allocate device

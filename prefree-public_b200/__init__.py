@@ -93,7 +93,8 @@ def _load():
         f.restype = st
     for name in ("pf_spmv_dist_f64_i64", "pf_spmv_dist_f64_i32"):
         f = getattr(lib, name)
-        f.argtypes = [vp, i64, i64, i64, vp, vp, vp, vp, vp, C.c_int, C.c_int, vp, vp, i64, vp]
+        f.argtypes = [vp, i64, i64, i64, vp, vp, vp, vp, vp, C.c_int, C.c_int, vp, vp, i64, vp,
+                      C.c_uint64, vp]
         f.restype = st
     lib.pf_spmv_noalloc_f64_i32.argtypes = [i64, i64, i64, vp, vp, vp, dbl, vp, dbl, vp, vp]
     lib.pf_spmv_noalloc_f64_i32.restype = st
@@ -236,11 +237,12 @@ def spmm(handle: Handle, m: int, n: int, nnz: int, row_ptr, col, val, X, Y,
 
 def spmv_dist(handle: Handle, m: int, n: int, nnz: int, row_ptr, col, val, x, prev_slots,
               nranks: int, rank: int, out_ptrs_dev: int, slot_ptrs_dev: int, row_offset: int,
-              stream=None):
+              stream=None, flag_ptrs_dev: int = 0, step: int = 0):
     """Fused multiply + all-gather step (see pf_spmv_dist_* in prefree_b200.h):
     this rank's rows of alpha*A*x go straight into every rank's next-x buffer
     (out_ptrs_dev: device array of nranks pointers), ||y||^2 into every rank's
-    slot `rank` (slot_ptrs_dev); alpha = 1/sqrt(sum(prev_slots))."""
+    slot `rank` (slot_ptrs_dev); alpha = 1/sqrt(sum(prev_slots)). With
+    flag_ptrs_dev the kernel also is the step barrier (step = 0, 1, ...)."""
     import torch
     if stream is None:
         stream = torch.cuda.current_stream().cuda_stream
@@ -249,7 +251,8 @@ def spmv_dist(handle: Handle, m: int, n: int, nnz: int, row_ptr, col, val, x, pr
     f = lib.pf_spmv_dist_f64_i64 if row_ptr.element_size() == 8 else lib.pf_spmv_dist_f64_i32
     _check(f(handle.ptr, int(m), int(n), int(nnz), _ptr(row_ptr), _ptr(col), _ptr(val), _ptr(x),
              _ptr(prev_slots), int(nranks), int(rank), C.c_void_p(int(out_ptrs_dev)),
-             C.c_void_p(int(slot_ptrs_dev)), int(row_offset), C.c_void_p(stream)))
+             C.c_void_p(int(slot_ptrs_dev)), int(row_offset),
+             C.c_void_p(int(flag_ptrs_dev) or None), int(step), C.c_void_p(stream)))
 
 
 def spmv_host(handle: Handle, row_ptr: np.ndarray, col: np.ndarray, val: np.ndarray,

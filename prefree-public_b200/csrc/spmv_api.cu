@@ -401,7 +401,9 @@ template <typename IT>
 static pf_status launch_dist(pf_handle h, int64_t m, int64_t n, int64_t nnz, const IT *row_ptr,
                              const int32_t *col, const double *val, const double *x,
                              const double *prev, int nranks, int rank, double *const *outs,
-                             double *const *slots, int64_t row_offset, cudaStream_t st) {
+                             double *const *slots, int64_t row_offset,
+                             unsigned long long *const *flags, unsigned long long step,
+                             cudaStream_t st) {
   PF_CHECK_ARG(h != nullptr, "null handle");
   PF_CHECK_ARG(m > 0 && n > 0 && nnz > 0, "empty shard");
   PF_CHECK_ARG(row_ptr && col && val && x && prev && outs && slots, "null pointer");
@@ -432,6 +434,8 @@ static pf_status launch_dist(pf_handle h, int64_t m, int64_t n, int64_t nnz, con
   D.row_offset = row_offset;
   D.nranks = nranks;
   D.rank = rank;
+  D.flags = flags;
+  D.step = step;
   switch (rowvec_lanes((double)nnz / (double)m)) {
     case 2: return launch_rowvec_dist<IT, 2>(h, prm, D, st);
     case 4: return launch_rowvec_dist<IT, 4>(h, prm, D, st);
@@ -949,18 +953,24 @@ pf_status pf_spmv_dist_f64_i64(pf_handle h, int64_t m, int64_t n, int64_t nnz,
                                const int64_t *row_ptr, const int32_t *col_idx,
                                const double *val, const double *x, const double *prev_slots,
                                int nranks, int rank, double *const *out_ptrs,
-                               double *const *slot_ptrs, int64_t row_offset, void *stream) {
+                               double *const *slot_ptrs, int64_t row_offset,
+                               uint64_t *const *flag_ptrs, uint64_t step, void *stream) {
   return launch_dist<int64_t>(h, m, n, nnz, row_ptr, col_idx, val, x, prev_slots, nranks, rank,
-                              out_ptrs, slot_ptrs, row_offset, (cudaStream_t)stream);
+                              out_ptrs, slot_ptrs, row_offset,
+                              reinterpret_cast<unsigned long long *const *>(flag_ptrs),
+                              (unsigned long long)step, (cudaStream_t)stream);
 }
 
 pf_status pf_spmv_dist_f64_i32(pf_handle h, int64_t m, int64_t n, int64_t nnz,
                                const int32_t *row_ptr, const int32_t *col_idx,
                                const double *val, const double *x, const double *prev_slots,
                                int nranks, int rank, double *const *out_ptrs,
-                               double *const *slot_ptrs, int64_t row_offset, void *stream) {
+                               double *const *slot_ptrs, int64_t row_offset,
+                               uint64_t *const *flag_ptrs, uint64_t step, void *stream) {
   return launch_dist<int32_t>(h, m, n, nnz, row_ptr, col_idx, val, x, prev_slots, nranks, rank,
-                              out_ptrs, slot_ptrs, row_offset, (cudaStream_t)stream);
+                              out_ptrs, slot_ptrs, row_offset,
+                              reinterpret_cast<unsigned long long *const *>(flag_ptrs),
+                              (unsigned long long)step, (cudaStream_t)stream);
 }
 
 PF_DEFINE_SPMV(f64_i32, double, int32_t)

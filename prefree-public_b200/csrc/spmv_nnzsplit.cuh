@@ -115,9 +115,28 @@ struct DistOut {
   const double *prev;    // this rank's copy of the previous iteration's slots
   double *cta_part;      // [grid] per-CTA partials
   unsigned *counter;     // zero between launches
+  // step barrier (optional): flags[p][q] = steps rank q has finished, as seen
+  // by rank p. Step `step` waits until this rank's flags reach `step` for
+  // every rank and, when done, sets flags[p][rank] = step + 1 on every p.
+  unsigned long long *const *flags;
+  unsigned long long step;
   int64_t row_offset;
   int nranks, rank;
 };
+
+// Bound of the step barrier's wait: far above any step (milliseconds); a
+// peer that never arrives makes the step flag PF_DEVERR_WAIT_TIMEOUT and go on.
+constexpr uint64_t PF_DIST_WAIT_NS = 1000000000ull;  // 1 s
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 
 
 // Smallest idx in [0, m] with row_ptr[idx] >= key (row_ptr[m] >= key assumed).

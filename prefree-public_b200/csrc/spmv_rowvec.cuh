@@ -16,6 +16,7 @@
 #pragma once
 
 #include "pf_common.cuh"
+#include "pf_ptx.cuh"
 #include "spmv_nnzsplit.cuh"
 
 namespace pf {
@@ -114,6 +115,12 @@ __device__ __forceinline__ void dist_norm_epilogue(const DistOut &D, double nsq)
     for (int w = 0; w < NTB / 32; ++w) tot += part[w];
     for (int p = 0; p < D.nranks; ++p) D.slots[p][D.rank] = tot;
     *D.counter = 0;
+    if (D.flags) {
+      // every CTA's stores are visible system-wide (each fenced before the
+      // count); announce this step to every rank
+      __threadfence_system();
+      for (int p = 0; p < D.nranks; ++p) st_release_sys(D.flags[p] + D.rank, D.step + 1);
+    }
   }
   __threadfence_system();
 }
@@ -197,6 +204,26 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
   __shared__ double *s_outs[DIST ? 64 : 1];
   __shared__ double s_wbuf[DIST ? NTB / 32 : 1][DIST ? SUPER : 1];  // a warp's super-chunk
   if (DIST) {
+    if (D.flags && D.step > 0) {
+      // step barrier: every rank has finished the previous step (its rows of
+      // this x and its norm slot are in place), waited on by one thread
+      if (threadIdx.x == 0) {
+        const unsigned long long *mine = D.flags[D.rank];
+        const uint64_t t0 = ptx::globaltimer_ns();
+        bool late = false;
+        for (int q = 0; q < D.nranks && !late; ++q) {
+          while (ld_acquire_sys(mine + q) < D.step) {
+            if (ptx::globaltimer_ns() - t0 > PF_DIST_WAIT_NS) {
+              atomicOr(P.err, PF_DEVERR_WAIT_TIMEOUT);
+              late = true;
+              break;
+            }
+            __nanosleep(256);
+          }
+        }
+      }
+      __syncthreads();
+    }
     double s = 0.0;
     for (int i = 0; i < D.nranks; ++i) s += D.prev[i];
     alpha = s > 0.0 ? 1.0 / sqrt(s) : 1.0;

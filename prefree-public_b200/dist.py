@@ -105,16 +105,18 @@ class FusedPowerIteration:
     The kernel (pf_spmv_dist_*) stores every finished row of this rank
     straight into every rank's next-x buffer over NVLink and reduces ||y||^2
     in the same pass; alpha = 1/||x_k|| is taken on the device from the norm
-    slots, so a step is one kernel plus one cross-rank barrier and the host
-    never waits for the GPU.
+    slots, and the kernel is also the step barrier (step counters in the same
+    memory), so a step is one kernel launch and the host never waits for the
+    GPU or for the other ranks.
 
     Buffers: one symmetric-memory allocation per rank (torch symmetric
     memory: every rank can address every other rank's copy) holding two x
-    buffers and two norm-slot arrays, used alternately: step k reads x[k%2]
-    and slots[k%2], writes x[(k+1)%2] and slots[(k+1)%2] on every rank. The
-    barrier after each step makes peers' stores visible and keeps any rank
-    from overwriting a buffer that another rank still reads. With one rank
-    the buffers are ordinary device memory and no barrier is needed.
+    buffers, two norm-slot arrays and the step counters. Step k reads x[k%2]
+    and slots[k%2] and writes x[(k+1)%2] and slots[(k+1)%2] on every rank; it
+    starts reading only when every rank has finished step k-1, which makes
+    peers' stores visible and keeps any rank from overwriting a buffer that
+    another rank still reads. With one rank the buffers are ordinary device
+    memory and there is nothing to wait for.
     """
 
     SLOTS = 64
@@ -131,7 +133,7 @@ class FusedPowerIteration:
         self.nnz = int(col.numel())
         self.stream = stream or torch.cuda.current_stream(x0.device)
         dev = x0.device
-        total = 2 * self.n + 2 * self.SLOTS
+        total = 2 * self.n + 3 * self.SLOTS  # x0, x1, slots0, slots1, step counters
         if world > 1:
             import torch.distributed as dist
             import torch.distributed._symmetric_memory as symm_mem
@@ -150,6 +152,11 @@ class FusedPowerIteration:
                                       device=dev) for k in (0, 1)]
         self.slot_ptrs = [torch.tensor([b + 8 * (2 * self.n + k * self.SLOTS) for b in bases],
                                        dtype=torch.int64, device=dev) for k in (0, 1)]
+        # step counters: uint64 words after the slots (zero: no step finished)
+        self.flags = self.buf[2 * self.n + 2 * self.SLOTS:2 * self.n + 3 * self.SLOTS]
+        self.flags.zero_()
+        self.flag_ptrs = torch.tensor([b + 8 * (2 * self.n + 2 * self.SLOTS) for b in bases],
+                                      dtype=torch.int64, device=dev) if world > 1 else None
         self.xs[0].copy_(x0)
         self.slots[0].zero_()
         self.slots[1].zero_()
@@ -165,9 +172,9 @@ class FusedPowerIteration:
                           self.xs[k % 2], self.slots[k % 2], self.world, self.rank,
                           self.out_ptrs[(k + 1) % 2].data_ptr(),
                           self.slot_ptrs[(k + 1) % 2].data_ptr(), self.row_offset,
-                          stream=self.stream)
-        if self.hdl is not None:
-            self.hdl.barrier(channel=0)
+                          stream=self.stream,
+                          flag_ptrs_dev=self.flag_ptrs.data_ptr() if self.flag_ptrs is not None else 0,
+                          step=k)
         self.k += 1
 
     @property
@@ -175,6 +182,14 @@ class FusedPowerIteration:
         """The current (unnormalised) iterate."""
         return self.xs[self.k % 2]
 
+    def sync(self):
+        """Wait until every rank has finished its steps so far (a collective:
+        every rank calls it): afterwards x and the norm slots are complete."""
+        self.torch.cuda.synchronize(self.buf.device)
+        if self.hdl is not None:
+            self.hdl.barrier(channel=0)
+
     def norm_sq(self) -> float:
-        """||A x_{k-1}||^2 of the last step (synchronizes)."""
+        """||A x_{k-1}||^2 of the last step (a collective: see sync)."""
+        self.sync()
         return float(self.slots[self.k % 2][:self.world].sum().item())

@@ -141,3 +141,37 @@ def test_two_gpus_fused_and_nccl_match_oracle(pf, oracle):
         assert close(xf, xr) and close(xu, xr), rank
         assert np.allclose(nf, nr, rtol=1e-12) and np.allclose(nu, nr, rtol=1e-12)
     assert np.array_equal(res[0][2], res[1][2])       # every rank holds the same x
+
+
+def test_step_barrier_times_out_without_peer(pf):
+    """The fused step's in-kernel barrier waits for every rank's previous step
+    with a bound: a step counter that nothing sets makes the kernel give up
+    after ~1 s, flag PF_DEVERR_WAIT_TIMEOUT and still finish (announcing its
+    own step). One GPU: the "second rank" is only memory here, no kernel of
+    it runs, so nothing waits on this kernel."""
+    import time
+    import torch
+    spec = small_spec(pf).resolved()
+    rp, col, val = pf.gen_rows_device(spec, index_dtype=torch.int64)
+    x = pf.gen_x_device(spec)
+    m, n = spec.m, spec.n
+    outs = [torch.zeros(n, dtype=torch.float64, device="cuda") for _ in range(2)]
+    slots = [torch.zeros(64, dtype=torch.float64, device="cuda") for _ in range(2)]
+    flags = [torch.zeros(64, dtype=torch.int64, device="cuda") for _ in range(2)]
+    prev = torch.zeros(64, dtype=torch.float64, device="cuda")
+    prev[0] = float(x.dot(x))
+    ptrs = lambda ts: torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device="cuda")
+    out_p, slot_p, flag_p = ptrs(outs), ptrs(slots), ptrs(flags)
+    h = pf.Handle()
+    t0 = time.time()
+    pf.spmv_dist(h, m, n, col.numel(), rp, col, val, x, prev, 2, 0, out_p.data_ptr(),
+                 slot_p.data_ptr(), 0, flag_ptrs_dev=flag_p.data_ptr(), step=1)
+    torch.cuda.synchronize()
+    waited = time.time() - t0
+    bits = h.device_error()
+    h.close()
+    assert bits & 1, f"expected the wait-timeout bit, got {bits:#x}"
+    assert 0.5 < waited < 30
+    # the step still ran and announced step 2 on both ranks' counters
+    assert int(flags[0][0]) == 2 and int(flags[1][0]) == 2
+    assert float(slots[0][0]) > 0 and float(slots[1][0]) == float(slots[0][0])
