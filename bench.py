@@ -278,6 +278,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--path", default="fused", choices=["fused", "nccl"],
                     help="power mode: fused multiply + all-gather kernel, or SpMV + NCCL")
+    ap.add_argument("--barrier", default="kernel", choices=["kernel", "host"],
+                    help="fused path: step barrier inside the kernel (step counters) "
+                         "or a symmetric-memory barrier launched between steps")
     ap.add_argument("--mode", default="power", choices=["power", "kernel"],
                     help="power: the config-5 power iteration (the benchmark line); "
                          "kernel: per-config single-GPU multiply timing")
@@ -359,7 +362,8 @@ def main():
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
-                fp = fused.flag_ptrs.data_ptr() if fused.flag_ptrs is not None else 0
+                fp = fused.flag_ptrs.data_ptr() if (fused.flag_ptrs is not None
+                                                    and args.barrier == "kernel") else 0
                 pf.spmv_dist(h, m_loc, n, nnz_loc, rp, col, val, fused.xs[fused.k % 2],
                              fused.slots[fused.k % 2], world, rank,
                              fused.out_ptrs[(fused.k + 1) % 2].data_ptr(),
@@ -367,6 +371,8 @@ def main():
                              stream=stream, flag_ptrs_dev=fp, step=fused.k)
                 e1.record(stream)
                 ev_pairs.append((e0, e1))
+                if fused.hdl is not None and not fp:
+                    fused.hdl.barrier(channel=0)
                 fused.k += 1
                 return None
         it = _Step()

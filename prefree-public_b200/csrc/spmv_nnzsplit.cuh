@@ -128,9 +128,12 @@ struct DistOut {
 // peer that never arrives makes the step flag PF_DEVERR_WAIT_TIMEOUT and go on.
 constexpr uint64_t PF_DIST_WAIT_NS = 1000000000ull;  // 1 s
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+// polling load: no ordering of its own (an acquire load per poll would
+// invalidate the SM's L1 under the CTAs that are already computing); the
+// waiter orders its later reads with one fence after the wait
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long *p) {
   unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 

@@ -212,7 +212,7 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
         const uint64_t t0 = ptx::globaltimer_ns();
         bool late = false;
         for (int q = 0; q < D.nranks && !late; ++q) {
-          while (ld_acquire_sys(mine + q) < D.step) {
+          while (ld_relaxed_sys(mine + q) < D.step) {
             if (ptx::globaltimer_ns() - t0 > PF_DIST_WAIT_NS) {
               atomicOr(P.err, PF_DEVERR_WAIT_TIMEOUT);
               late = true;
@@ -221,6 +221,7 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
             __nanosleep(256);
           }
         }
+        __threadfence_system();  // the peers' stores before this CTA's reads
       }
       __syncthreads();
     }
