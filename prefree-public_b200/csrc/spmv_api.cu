@@ -40,11 +40,10 @@ void count_launches(unsigned long long k) { count_launch(k); }
 
 }  // namespace pf
 
-// Per-device state: scratch for cut-row carries, error word, cached buffers
-// for the host-buffer entry points.
+// The selector's decision for one matrix.
 struct pf_variant_choice {
-  int variant;  // PF_VARIANT_NNZSPLIT / ROWGROUP / NNZSPLIT_LDG
-  int lanes;    // ROWGROUP lanes per row
+  int variant;  // a PF_VARIANT_* other than AUTO
+  int lanes;    // lanes per row for the row-group variants (ROWVEC, ROWGROUP, ROWSTREAM)
 };
 
 struct pf_select_entry {
@@ -54,6 +53,9 @@ struct pf_select_entry {
   pf_variant_choice choice;
 };
 
+// Per-device state: the selector cache, scratch for cut-row carries and the
+// long-row chunks, the fused step's norm partials, the device error word, and
+// the buffers of the host-buffer entry points.
 struct pf_handle_s {
   int device = 0;
   int num_sms = 0;
@@ -64,14 +66,15 @@ struct pf_handle_s {
   int cache_n = 0, cache_next = 0;
   int64_t *sample_dev = nullptr;
   int64_t *sample_host = nullptr;  // pinned
-  int64_t slice_override = 0;  // testing knob: fixed nnz per CTA slice
+  int64_t slice_override = 0;  // testing knob: fixed nnz per slice (NNZSPLIT*, WARPSPLIT)
   // cut-row scratch
   double *carry = nullptr;     // 2 * cap doubles (head, tail)
   unsigned *counters = nullptr;
   int64_t cap = 0;
   bool scratch_dirty = false;
   unsigned *err = nullptr;
-  // long-row escape list (ROWVEC_LX), one allocation, zeroed when grown
+  // long-row chunk descriptors (ROWVEC_LX, ROWSTREAM_LX), one allocation,
+  // counters zeroed when grown
   void *lx_buf = nullptr;
   size_t lx_bytes = 0;
   bool lx_dirty = false;
@@ -165,20 +168,26 @@ static int nnzsplit_occupancy() {
   return occ;
 }
 
+// Kernels with more than 48 KB of dynamic shared memory need the attribute
+// set on every device they run on: occupancy and attribute are set up once
+// per device (0 = not yet).
+constexpr int kMaxDevices = 64;
+
 template <typename VT, typename IT>
-static int tma_occupancy(size_t *smem_out) {
+static int tma_occupancy(int dev, size_t *smem_out) {
   using C = TmaCfgDefault;
-  static int occ = -1;
+  static int occ[kMaxDevices] = {};
   const size_t smem = sizeof(TmaSmem<VT, IT, C>);
-  if (occ < 0) {
+  int &o = occ[dev % kMaxDevices];
+  if (o == 0) {
     cudaFuncSetAttribute(spmv_tma_kernel<VT, IT, C>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    int o = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, spmv_tma_kernel<VT, IT, C>, C::NT, smem);
-    occ = std::max(1, o);
+    int v = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, spmv_tma_kernel<VT, IT, C>, C::NT, smem);
+    o = std::max(1, v);
   }
   *smem_out = smem;
-  return occ;
+  return o;
 }
 
 // ---- variant selection from sampled row lengths ------------------------------
@@ -336,11 +345,11 @@ template <typename VT, typename IT, int V>
 static pf_status launch_rowstream(pf_handle h, const SpmvParams<VT, IT> &prm, bool lx,
                                   cudaStream_t st) {
   using C = RowStreamCfg;
-  static int occ[2] = {-1, -1};
+  static int occ[kMaxDevices][2] = {};
   const size_t smem = sizeof(RowStreamSmem<VT, IT>);
   auto kern = lx ? spmv_rowstream_kernel<VT, IT, V, true> : spmv_rowstream_kernel<VT, IT, V, false>;
-  int &o = occ[lx ? 1 : 0];
-  if (o < 0) {
+  int &o = occ[h->device % kMaxDevices][lx ? 1 : 0];
+  if (o == 0) {
     PF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int v = 0;
     PF_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kern, C::NTP, smem));
@@ -570,7 +579,7 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
   int occ;
   if constexpr (!kHalf) {
     if (tma) {
-      occ = tma_occupancy<VT, IT>(&smem);
+      occ = tma_occupancy<VT, IT>(h->device, &smem);
       min_T = 2 * TmaCfgDefault::TILE;
     }
   }
@@ -608,10 +617,9 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
   return PF_OK;
 }
 
-// WARPSPLIT: one wave of resident CTAs, one equal-nnz slice per warp (at
-// least one 256-non-zero tile each).
-template <typename VT, typename IT>
-static pf_status launch_warpsplit(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st) {
+// WARPSPLIT shape: row_ptr window, ring stages, CTAs per SM, non-zeros per
+// lane. The defaults are the best of sweeps on the configs (compile with -D
+// to sweep them).
 #ifndef PF_WS_WIN
 #define PF_WS_WIN 128
 #endif
@@ -624,11 +632,17 @@ static pf_status launch_warpsplit(pf_handle h, SpmvParams<VT, IT> prm, cudaStrea
 #ifndef PF_WS_EPL
 #define PF_WS_EPL 8
 #endif
+
+// WARPSPLIT: one wave of resident CTAs, one equal-nnz slice per warp (at
+// least one tile each).
+template <typename VT, typename IT>
+static pf_status launch_warpsplit(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st) {
   constexpr int NTB = 256, WIN = PF_WS_WIN, NS = PF_WS_NS, MINB = PF_WS_MINB, EPL = PF_WS_EPL;
   auto kern = spmv_warpsplit_kernel<VT, IT, NTB, WIN, NS, MINB, EPL>;
   const size_t smem = sizeof(WarpSplitSmem<VT, WIN, NS, EPL>) * (NTB / 32);
-  static int occ = -1;
-  if (occ < 0) {
+  static int occ_dev[kMaxDevices] = {};
+  int &occ = occ_dev[h->device % kMaxDevices];
+  if (occ == 0) {
     PF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int o = 0;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, NTB, smem);

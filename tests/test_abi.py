@@ -76,3 +76,32 @@ def test_shard_bounds(pf):
     for k in range(1, 3):
         assert rp[b[k]] >= 30 * k // 3 and (b[k] == 0 or rp[b[k] - 1] < 30 * k // 3)
     assert np.array_equal(pf.shard_bounds(rp.astype(np.int32), 3), b)
+
+
+def test_invalid_arguments_return_status_not_crash(pf):
+    """Argument checks run on the host before any device work: a null handle,
+    negative sizes or a bad variant return PF_ERR_INVALID (1) with a message,
+    as the reference's callers would otherwise meet an exit() or a fault."""
+    lib = pf.lib
+    null = C.c_void_p()
+    assert lib.pf_spmv_f64_i32(null, 4, 4, 0, None, None, None, 1.0, None, 0.0, None, None) == 1
+    assert b"null handle" in lib.pf_last_error()
+    assert lib.pf_spmv_f16_i64(null, 4, 4, 0, None, None, None, 1.0, None, 0.0, None, None) == 1
+    assert lib.pf_spmm_f64_i32(null, 4, 4, 0, None, None, None, 2, 1.0, None, 2, 0.0, None, 2,
+                               None) == 1
+    assert lib.pf_handle_set_variant(null, 0) == 1
+    assert lib.pf_spmv_dist_f64_i64(null, 4, 4, 4, None, None, None, None, None, 1, 0, None,
+                                    None, 0, None, 0, None) == 1
+    t, p = C.c_double(), C.c_double()
+    assert lib.pf_prefree_spmv_f64_i32(None, None, None, None, None, -1, 4, 0,
+                                       C.byref(t), C.byref(p)) == 1
+    assert b"negative" in lib.pf_last_error()
+
+
+def test_shard_bounds_equal_nnz(pf):
+    rp = np.array([0, 3, 3, 10, 11, 20], dtype=np.int64)
+    b = pf.shard_bounds(rp, 3)
+    assert b[0] == 0 and b[-1] == 5 and list(b) == sorted(b)
+    # every boundary is the first row whose start reaches k * nnz / parts
+    for k in range(1, 3):
+        assert b[k] == int(np.searchsorted(rp, k * 20 // 3))
