@@ -189,6 +189,60 @@ __device__ __forceinline__ int32_t ldg_hint<int32_t>(const int32_t *p, uint64_t 
   return v;
 }
 
+// x gathers: read-only loads that ask L2 for a 64-byte fill on a miss. A
+// random 8-byte gather into a vector far larger than L2 then costs ~58 DRAM
+// bytes instead of the ~107 of the default fill (measured on B200: 81.7 M vs
+// 145.6 M sectors for 41.9 M gathers into 512 MB); hits are unchanged.
+template <typename T>
+__device__ __forceinline__ T ldg_x(const T *p);
+
+template <>
+__device__ __forceinline__ double ldg_x<double>(const double *p) {
+  double v;
+  asm("ld.global.nc.L2::64B.f64 %0, [%1];" : "=d"(v) : "l"(p));
+  return v;
+}
+
+template <>
+__device__ __forceinline__ float ldg_x<float>(const float *p) {
+  float v;
+  asm("ld.global.nc.L2::64B.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+
+template <typename H>
+__device__ __forceinline__ H ldg_x_16(const H *p) {
+  unsigned short v;
+  asm("ld.global.nc.L2::64B.b16 %0, [%1];" : "=h"(v) : "l"(p));
+  return half_from_bits<H>(v);
+}
+
+template <>
+__device__ __forceinline__ __half ldg_x<__half>(const __half *p) {
+  return ldg_x_16(p);
+}
+
+template <>
+__device__ __forceinline__ __nv_bfloat16 ldg_x<__nv_bfloat16>(const __nv_bfloat16 *p) {
+  return ldg_x_16(p);
+}
+
+// 16-byte pieces of a dense row gathered by column index (SpMM's X rows),
+// with the same 64-byte fill
+__device__ __forceinline__ double2 ldg_x_v2(const double2 *p) {
+  double2 v;
+  asm("ld.global.nc.L2::64B.v2.f64 {%0, %1}, [%2];" : "=d"(v.x), "=d"(v.y) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ float4 ldg_x_v4(const float4 *p) {
+  float4 v;
+  asm("ld.global.nc.L2::64B.v4.f32 {%0, %1, %2, %3}, [%4];"
+      : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+      : "l"(p));
+  return v;
+}
+
 // 16-bit values: a 16-bit load of the bit pattern
 template <typename H>
 __device__ __forceinline__ H ldg_hint_16(const H *p, uint64_t policy) {

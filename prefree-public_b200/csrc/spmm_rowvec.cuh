@@ -36,12 +36,13 @@ struct SpmmParams {
 };
 
 // KC values of an X row: 16-byte loads when the row starts on a 16-byte
-// boundary (VX), single elements otherwise
+// boundary (VX), single elements otherwise; every load asks L2 for a 64-byte
+// fill, so a random row gather does not drag in the neighbouring row
 template <typename VT, int KC, bool VX>
 struct XRow {
   __device__ __forceinline__ static void load(const VT *xr, int kc, double out[KC]) {
 #pragma unroll
-    for (int j = 0; j < KC; ++j) out[j] = j < kc ? (double)__ldg(xr + j) : 0.0;
+    for (int j = 0; j < KC; ++j) out[j] = j < kc ? (double)ptx::ldg_x(xr + j) : 0.0;
   }
 };
 template <int KC>
@@ -50,7 +51,7 @@ struct XRow<double, KC, true> {
 #pragma unroll
     for (int j = 0; j < KC; j += 2) {
       double2 t = make_double2(0.0, 0.0);
-      if (j < kc) t = __ldg(reinterpret_cast<const double2 *>(xr + j));
+      if (j < kc) t = ptx::ldg_x_v2(reinterpret_cast<const double2 *>(xr + j));
       out[j] = t.x;
       if (j + 1 < KC) out[j + 1] = t.y;
     }
@@ -62,7 +63,7 @@ struct XRow<float, KC, true> {
 #pragma unroll
     for (int j = 0; j < KC; j += 4) {
       float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (j < kc) t = __ldg(reinterpret_cast<const float4 *>(xr + j));
+      if (j < kc) t = ptx::ldg_x_v4(reinterpret_cast<const float4 *>(xr + j));
       const float v[4] = {t.x, t.y, t.z, t.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i)

@@ -311,7 +311,7 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
           const bool use = el >= lo[u] && el < len[u];
           const bool inb = (uint32_t)cc[i] < n;
           bad |= use && !inb;
-          xv[u][i] = (use && inb) ? __ldg(P.x + cc[i]) : VT(0);
+          xv[u][i] = (use && inb) ? ptx::ldg_x(P.x + cc[i]) : VT(0);
         }
       }
       more = false;
@@ -415,7 +415,7 @@ spmv_longrow_chunks_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L) {
           const bool use = q + i >= lo && q + i < hi;
           const bool inb = (uint32_t)cc[i] < n;
           bad |= use && !inb;
-          xv[j][i] = (use && inb) ? __ldg(P.x + cc[i]) : VT(0);
+          xv[j][i] = (use && inb) ? ptx::ldg_x(P.x + cc[i]) : VT(0);
         }
       }
 #pragma unroll

@@ -284,7 +284,7 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
         const bool use = lo + q >= ga && lo + q < gb;
         const bool inb = (uint32_t)cc[q] < n;
         bad |= use && !inb;
-        xv[q] = (use && inb) ? __ldg(P.x + cc[q]) : VT(0);
+        xv[q] = (use && inb) ? ptx::ldg_x(P.x + cc[q]) : VT(0);
       }
     };
     if (!wait_tile(0)) return;
