@@ -17,7 +17,10 @@
 // lane the sum flowing into its first row from the lanes before it (and from
 // earlier tiles). A tile without a row end is one warp sum. When more than
 // WIN rows end inside a tile, the tile is walked in several passes, one per
-// window.
+// window. A whole tile whose row ends are distinct and all in the window
+// skips the search: a bit per non-zero marks the row ends, every lane walks
+// its products without branches, and the tile's rows leave together in one
+// coalesced store (the same sums in the same order).
 //
 // A row that starts before the slice (head) or runs past its end (tail) is
 // finished by the last of its slices to deposit its partial, summing the
@@ -37,6 +40,11 @@
 #include "pf_ptx.cuh"
 #include "spmv_nnzsplit.cuh"
 #include "spmv_tma.cuh"
+
+// the fast tile walk (0: every tile takes the searching pass)
+#ifndef PF_WS_FAST
+#define PF_WS_FAST 1
+#endif
 
 namespace pf {
 
@@ -60,6 +68,10 @@ struct WarpSplitSmem {
   Stage st[NS];
   int win[WIN];
   uint64_t bar[NS];
+  // fast tile walk: the sums of the rows ending in the tile, in row order,
+  // and one bit per non-zero (set where a row ends after it)
+  alignas(16) double out[32 * EPL];
+  uint32_t ends[EPL];
 };
 
 // Positions inside a slice are 32-bit offsets from its first non-zero S0
@@ -247,6 +259,90 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
       return moved;
     };
 
+    // Fast walk of a full tile whose row ends all lie in the window and are
+    // distinct (no empty row ends inside it): a bit per non-zero marks the
+    // row ends, each lane walks its EPL products without searching the
+    // window, rows that end inside a lane go to shared memory by their rank
+    // in the tile, and the tile's rows are written together at the end. The
+    // same sums in the same order as pass(). False (nothing changed) when the
+    // tile does not qualify.
+    auto fast_tile = [&](int tb, const double(&p)[EPL]) -> bool {
+      const int tend = tb + TILE;
+      if (!PF_WS_FAST || tb < 0 || tend > L || g != tb || E[off] <= tb || E[WIN - 1] <= tend)
+        return false;
+      uint32_t *M = S.ends;
+      double *O = S.out;
+      if (lane < EPL) M[lane] = 0u;
+      __syncwarp();
+      int nend = 0;
+      bool odd = false;  // an end outside (tb, tend] or not above the one before
+      for (int j0 = off; j0 < WIN; j0 += 32) {
+        const int j = j0 + lane;
+        const int e = j < WIN ? E[j] : NEVER;
+        const bool in = e <= tend;
+        const int prev = (in && j > off) ? E[j - 1] : tb;
+        odd |= in && (e <= tb || e <= prev);
+        if (in && e > tb) atomicOr(&M[(e - 1 - tb) >> 5], 1u << ((e - 1 - tb) & 31));
+        const unsigned inb = __ballot_sync(0xffffffffu, in);
+        nend += __popc(inb);
+        if (!(inb >> 31)) break;
+      }
+      if (__any_sync(0xffffffffu, odd)) return false;
+      __syncwarp();
+      constexpr uint32_t LMASK = EPL >= 32 ? 0xffffffffu : ((1u << EPL) - 1u);
+      const uint32_t bits = (M[(lane * EPL) >> 5] >> ((lane * EPL) & 31)) & LMASK;
+      // rank of this lane's first row end among the tile's
+      const int cnt = __popc(bits);
+      int k = cnt;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, k, d);
+        if (lane >= d) k += t;
+      }
+      k -= cnt;
+      double acc = 0.0, head = 0.0;
+      int first = -1;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) {
+        acc += p[i];
+        const bool e = (bits >> i) & 1u;
+        const bool fst = e && first < 0;
+        if (e && !fst) O[k] = acc;
+        head = fst ? acc : head;
+        first = fst ? k : first;
+        acc = e ? 0.0 : acc;
+        k += e ? 1 : 0;
+      }
+      // segmented scan over lanes, as in pass()
+      int f = first >= 0 ? 1 : 0;
+      double v = acc;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int fu = __shfl_up_sync(0xffffffffu, f, d);
+        const double vu = __shfl_up_sync(0xffffffffu, v, d);
+        if (lane >= d) {
+          if (!f) v = vu + v;
+          f |= fu;
+        }
+      }
+      const double incl = f ? v : carry + v;
+      double excl = __shfl_up_sync(0xffffffffu, incl, 1);
+      if (lane == 0) excl = carry;
+      if (first >= 0) O[first] = excl + head;
+      carry = __shfl_sync(0xffffffffu, incl, 31);
+      __syncwarp();
+      for (int j = lane; j < nend; j += 32) {
+        const int64_t R = rw + off + j;
+        if (R == head_row) contribute_cut_row(P, base, R, true, c, O[j]);
+        else write_row(R, O[j]);
+      }
+      __syncwarp();
+      off += nend;
+      rstart = E[off - 1];
+      g = tend;
+      return true;
+    };
+
     // Wait for tile i of the slice (every lane waits; the outcome is made
     // the same for the whole warp). On a copy that never lands: flag it, wait
     // (bounded) for this warp's other copies in flight, and report false.
@@ -353,7 +449,7 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
         for (int d = 16; d > 0; d >>= 1) t += __shfl_xor_sync(0xffffffffu, t, d);
         carry += t;
         g = tend;
-      } else {
+      } else if (!fast_tile(tb, p)) {
         const int g0 = g;
         while (g < tend) {
           if (off >= WIN / 2) load_window();
