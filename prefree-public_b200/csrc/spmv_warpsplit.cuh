@@ -259,35 +259,48 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
       return moved;
     };
 
-    // Fast walk of a full tile whose row ends all lie in the window and are
-    // distinct (no empty row ends inside it): a bit per non-zero marks the
-    // row ends, each lane walks its EPL products without searching the
-    // window, rows that end inside a lane go to shared memory by their rank
-    // in the tile, and the tile's rows are written together at the end. The
-    // same sums in the same order as pass(). False (nothing changed) when the
-    // tile does not qualify.
+    // Fast walk of a full tile whose row ends are distinct (no empty row
+    // ends inside it): a bit per non-zero marks the row ends, each lane walks
+    // its EPL products without searching the window, rows that end inside a
+    // lane go to shared memory by their rank in the tile, and the tile's rows
+    // are written together at the end. Row ends past the window are read from
+    // row_ptr directly (a tile of rows of one non-zero has 32 * EPL ends).
+    // The same sums in the same order as pass(). False (nothing changed) when
+    // the tile does not qualify.
     auto fast_tile = [&](int tb, const double(&p)[EPL]) -> bool {
       const int tend = tb + TILE;
-      if (!PF_WS_FAST || tb < 0 || tend > L || g != tb || E[off] <= tb || E[WIN - 1] <= tend)
-        return false;
+      if (!PF_WS_FAST || tb < 0 || tend > L || g != tb || E[off] <= tb) return false;
       uint32_t *M = S.ends;
       double *O = S.out;
       if (lane < EPL) M[lane] = 0u;
       __syncwarp();
       int nend = 0;
-      bool odd = false;  // an end outside (tb, tend] or not above the one before
-      for (int j0 = off; j0 < WIN; j0 += 32) {
+      int last_e = tb;  // the last row end in the tile
+      int prev_hi = tb;  // the end before this step's first
+      for (int j0 = off;; j0 += 32) {
         const int j = j0 + lane;
-        const int e = j < WIN ? E[j] : NEVER;
+        int e;
+        if (j < WIN) {
+          e = E[j];
+        } else {
+          const int64_t r1 = rw + 1 + j;
+          e = r1 <= P.m ? (int)max(min((int64_t)__ldg(P.row_ptr + r1) - S0, (int64_t)NEVER),
+                                   (int64_t)-1)
+                        : NEVER;
+        }
         const bool in = e <= tend;
-        const int prev = (in && j > off) ? E[j - 1] : tb;
-        odd |= in && (e <= tb || e <= prev);
+        int prev = __shfl_up_sync(0xffffffffu, e, 1);
+        if (lane == 0) prev = prev_hi;
+        // an end outside (tb, tend] or not above the one before: not this path
+        const bool odd = in && (e <= tb || e <= prev);
         if (in && e > tb) atomicOr(&M[(e - 1 - tb) >> 5], 1u << ((e - 1 - tb) & 31));
         const unsigned inb = __ballot_sync(0xffffffffu, in);
         nend += __popc(inb);
+        if (__any_sync(0xffffffffu, odd) || nend > TILE) return false;
+        if (inb) last_e = __shfl_sync(0xffffffffu, e, 31 - __clz(inb));
         if (!(inb >> 31)) break;
+        prev_hi = __shfl_sync(0xffffffffu, e, 31);
       }
-      if (__any_sync(0xffffffffu, odd)) return false;
       __syncwarp();
       constexpr uint32_t LMASK = EPL >= 32 ? 0xffffffffu : ((1u << EPL) - 1u);
       const uint32_t bits = (M[(lane * EPL) >> 5] >> ((lane * EPL) & 31)) & LMASK;
@@ -337,8 +350,8 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
         else write_row(R, O[j]);
       }
       __syncwarp();
-      off += nend;
-      rstart = E[off - 1];
+      off += nend;  // may pass the window: the next tile reloads it
+      rstart = last_e;
       g = tend;
       return true;
     };
@@ -375,12 +388,22 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
         cc[4 * b + 2] = c4.z;
         cc[4 * b + 3] = c4.w;
       }
+      if (ga == tb && gb == tb + TILE) {
+        // the whole tile lies in the slice
 #pragma unroll
-      for (int q = 0; q < EPL; ++q) {
-        const bool use = lo + q >= ga && lo + q < gb;
-        const bool inb = (uint32_t)cc[q] < n;
-        bad |= use && !inb;
-        xv[q] = (use && inb) ? ptx::ldg_x(P.x + cc[q]) : VT(0);
+        for (int q = 0; q < EPL; ++q) {
+          const bool inb = (uint32_t)cc[q] < n;
+          bad |= !inb;
+          xv[q] = inb ? ptx::ldg_x(P.x + cc[q]) : VT(0);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < EPL; ++q) {
+          const bool use = lo + q >= ga && lo + q < gb;
+          const bool inb = (uint32_t)cc[q] < n;
+          bad |= use && !inb;
+          xv[q] = (use && inb) ? ptx::ldg_x(P.x + cc[q]) : VT(0);
+        }
       }
     };
     if (!wait_tile(0)) return;
@@ -396,6 +419,7 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
       double p[EPL];
       {
         const int ga = max(tb, 0);
+        const bool full = tb >= 0 && tb + TILE <= L;
 #pragma unroll
         for (int h = 0; h < EPL / VB; ++h) {
           VT vv[VB];
@@ -419,10 +443,12 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
             vv[2] = t.z;
             vv[3] = t.w;
           }
+          // values outside the tile's part of the slice are not copied: a
+          // partial tile masks them
 #pragma unroll
           for (int e = 0; e < VB; ++e) {
             const int q = VB * h + e;
-            const bool use = lo + q >= ga && lo + q < tend;
+            const bool use = full || (lo + q >= ga && lo + q < tend);
             p[q] = use ? (double)vv[e] * (double)xv[q] : 0.0;
           }
         }
