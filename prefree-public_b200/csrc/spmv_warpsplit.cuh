@@ -18,9 +18,8 @@
 // earlier tiles). A tile without a row end is one warp sum. When more than
 // WIN rows end inside a tile, the tile is walked in several passes, one per
 // window. A whole tile whose row ends are distinct and all in the window
-// skips the search: a bit per non-zero marks the row ends, every lane walks
-// its products without branches, and the tile's rows leave together in one
-// coalesced store (the same sums in the same order).
+// skips the search: a bit per non-zero marks the row ends and every lane
+// walks its products against its bits (the same sums in the same order).
 //
 // A row that starts before the slice (head) or runs past its end (tail) is
 // finished by the last of its slices to deposit its partial, summing the
@@ -68,9 +67,9 @@ struct WarpSplitSmem {
   Stage st[NS];
   int win[WIN];
   uint64_t bar[NS];
-  // fast tile walk: the sums of the rows ending in the tile, in row order,
-  // and one bit per non-zero (set where a row ends after it)
-  alignas(16) double out[32 * EPL];
+  // fast tile walk: one bit per non-zero, set where a row ends after it (a
+  // row-sum buffer here would cost L1: shared memory and L1 share the SM's
+  // 256 KB, and config 3 slowed from 249 to 350 us with 2 KB more per warp)
   uint32_t ends[EPL];
 };
 
@@ -260,18 +259,16 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
     };
 
     // Fast walk of a full tile whose row ends are distinct (no empty row
-    // ends inside it): a bit per non-zero marks the row ends, each lane walks
-    // its EPL products without searching the window, rows that end inside a
-    // lane go to shared memory by their rank in the tile, and the tile's rows
-    // are written together at the end. Row ends past the window are read from
-    // row_ptr directly (a tile of rows of one non-zero has 32 * EPL ends).
-    // The same sums in the same order as pass(). False (nothing changed) when
-    // the tile does not qualify.
+    // ends inside it): a bit per non-zero marks the row ends, and each lane
+    // walks its EPL products without searching the window, writing the rows
+    // that end inside its range (a row's number is its rank among the tile's
+    // ends). Row ends past the window are read from row_ptr directly (a tile
+    // of rows of one non-zero has 32 * EPL ends). The same sums in the same
+    // order as pass(). False (nothing changed) when the tile does not qualify.
     auto fast_tile = [&](int tb, const double(&p)[EPL]) -> bool {
       const int tend = tb + TILE;
       if (!PF_WS_FAST || tb < 0 || tend > L || g != tb || E[off] <= tb) return false;
       uint32_t *M = S.ends;
-      double *O = S.out;
       if (lane < EPL) M[lane] = 0u;
       __syncwarp();
       int nend = 0;
@@ -313,6 +310,7 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
         if (lane >= d) k += t;
       }
       k -= cnt;
+      const int64_t R0 = rw + off;  // the row of rank 0
       double acc = 0.0, head = 0.0;
       int first = -1;
 #pragma unroll
@@ -320,7 +318,7 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
         acc += p[i];
         const bool e = (bits >> i) & 1u;
         const bool fst = e && first < 0;
-        if (e && !fst) O[k] = acc;
+        if (e && !fst) write_row(R0 + k, acc);
         head = fst ? acc : head;
         first = fst ? k : first;
         acc = e ? 0.0 : acc;
@@ -341,15 +339,14 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
       const double incl = f ? v : carry + v;
       double excl = __shfl_up_sync(0xffffffffu, incl, 1);
       if (lane == 0) excl = carry;
-      if (first >= 0) O[first] = excl + head;
-      carry = __shfl_sync(0xffffffffu, incl, 31);
-      __syncwarp();
-      for (int j = lane; j < nend; j += 32) {
-        const int64_t R = rw + off + j;
-        if (R == head_row) contribute_cut_row(P, base, R, true, c, O[j]);
-        else write_row(R, O[j]);
+      // a lane's first row is the only one that can be the slice's cut head
+      if (first >= 0) {
+        const int64_t R = R0 + first;
+        if (R == head_row) contribute_cut_row(P, base, R, true, c, excl + head);
+        else write_row(R, excl + head);
       }
-      __syncwarp();
+      carry = __shfl_sync(0xffffffffu, incl, 31);
+      __syncwarp();  // the mask is rewritten by the next tile
       off += nend;  // may pass the window: the next tile reloads it
       rstart = last_e;
       g = tend;
