@@ -17,9 +17,10 @@
 // lane the sum flowing into its first row from the lanes before it (and from
 // earlier tiles). A tile without a row end is one warp sum. When more than
 // WIN rows end inside a tile, the tile is walked in several passes, one per
-// window. A whole tile whose row ends are distinct and all in the window
-// skips the search: a bit per non-zero marks the row ends and every lane
-// walks its products against its bits (the same sums in the same order).
+// window. A whole tile whose row ends are distinct (no empty row ends inside
+// it) skips the search: a bit per non-zero marks the row ends, read from the
+// window and past it from row_ptr, and every lane walks its products against
+// its bits (the same sums in the same order).
 //
 // A row that starts before the slice (head) or runs past its end (tail) is
 // finished by the last of its slices to deposit its partial, summing the
@@ -313,16 +314,28 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
       const int64_t R0 = rw + off;  // the row of rank 0
       double acc = 0.0, head = 0.0;
       int first = -1;
-#pragma unroll
-      for (int i = 0; i < EPL; ++i) {
+      // one step of the walk; a row that ends here and is not the lane's
+      // first is written at once (its number is R0 + its rank)
+      auto step = [&](int i, auto store) {
         acc += p[i];
         const bool e = (bits >> i) & 1u;
         const bool fst = e && first < 0;
-        if (e && !fst) write_row(R0 + k, acc);
+        if (e && !fst) store(R0 + k, acc);
         head = fst ? acc : head;
         first = fst ? k : first;
         acc = e ? 0.0 : acc;
         k += e ? 1 : 0;
+      };
+      // beta is the same for the whole launch: the common beta = 0 walk
+      // stores without testing it or reading y
+      if (beta == 0.0) {
+        VT *const yv = P.y;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i)
+          step(i, [&](int64_t R, double v) { yv[R] = (VT)(alpha * v); });
+      } else {
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) step(i, write_row);
       }
       // segmented scan over lanes, as in pass()
       int f = first >= 0 ? 1 : 0;
