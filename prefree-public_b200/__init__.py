@@ -287,17 +287,48 @@ def preFreeSpMV(csrVal: np.ndarray, csrRowPtr: np.ndarray, csrColInd: np.ndarray
 # ---------------------------------------------------------------------------
 # Matrix Market input path and sharding
 # ---------------------------------------------------------------------------
+class _LibBuffer:
+    """An array the library allocated (pf_mmio_read, pf_csr_read), exposed to
+    numpy without a copy and handed back to pf_free when the last array that
+    views it is gone."""
+
+    def __init__(self, addr: int, n: int, typestr: str):
+        self._addr = addr
+        self.__array_interface__ = {"data": (addr, False), "shape": (n,),
+                                    "typestr": typestr, "version": 3}
+
+    def __del__(self):
+        addr, self._addr = self._addr, None
+        if addr:
+            try:
+                lib.pf_free(addr)
+            except Exception:  # interpreter shutdown: the process frees it
+                pass
+
+
+def _owned_array(ptr: C.c_void_p, n: int, dtype) -> np.ndarray:
+    addr = ptr.value
+    if not addr or n == 0:
+        if addr:
+            lib.pf_free(addr)
+        return np.empty(n, dtype=dtype)
+    return np.asarray(_LibBuffer(addr, n, np.dtype(dtype).str))
+
+
 def _take_csr(m, n, z, sym, rp, ci, va):
+    """The CSR arrays a library call returned, as numpy arrays that own them
+    (no copy: a copy of a large fresh array can cost seconds of page faults)."""
+    bufs = [(rp, m.value + 1, np.int64), (ci, z.value, np.int32), (va, z.value, np.float64)]
+    out = []
     try:
-        row_ptr = np.ctypeslib.as_array(C.cast(rp, C.POINTER(C.c_int64)), (m.value + 1,)).copy()
-        col = np.ctypeslib.as_array(C.cast(ci, C.POINTER(C.c_int32)), (max(z.value, 1),))[
-            :z.value].copy()
-        val = np.ctypeslib.as_array(C.cast(va, C.POINTER(C.c_double)), (max(z.value, 1),))[
-            :z.value].copy()
+        for ptr, cnt, dt in bufs:
+            out.append(_owned_array(ptr, cnt, dt))
+            ptr.value = None
     finally:
-        lib.pf_free(rp)
-        lib.pf_free(ci)
-        lib.pf_free(va)
+        for ptr, _, _ in bufs:
+            if ptr.value:
+                lib.pf_free(ptr.value)
+    row_ptr, col, val = out
     return m.value, n.value, z.value, bool(sym.value), row_ptr, col, val
 
 

@@ -16,20 +16,28 @@
 //   * CSR by counting sort in file order: entry k lands in row i after every
 //     earlier entry of row i, and its mirror lands in row j right after that
 //     (:1650-1695). Column order inside a row is therefore file order.
-// Differences: int64 row_ptr/nnz, the entry lines are parsed by several
-// threads, dense "array" files and malformed input return an error instead of
-// reading garbage.
+// Differences: int64 row_ptr/nnz; the file is read, the entry lines parsed
+// and the CSR built by several threads (the CSR build stays in file order:
+// each thread owns a range of rows and places its entries in file order);
+// dense "array" files and malformed input return an error instead of reading
+// garbage.
 #include <algorithm>
 #include <cctype>
 #include <cerrno>
+#include <charconv>
+#include <climits>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <memory>
 #include <string>
 #include <thread>
 #include <vector>
 
+#include <fcntl.h>
 #include <sys/stat.h>
+#include <unistd.h>
 
 #include "../../include/prefree_b200.h"
 
@@ -40,9 +48,51 @@ void set_error(const char *fmt, ...);
 namespace {
 
 struct Entries {
-  std::vector<int32_t> ri, ci;
-  std::vector<double> v;
+  std::unique_ptr<int32_t[]> ri, ci;  // left uninitialised: every slot is written
+  std::unique_ptr<double[]> v;
 };
+
+// strtoll on a token, without copying it: optional sign, then base-10 digits
+// up to the first other character; saturates like strtoll. False when no
+// digit follows the sign.
+inline bool parse_ll(const char *s, const char *e, long long *out) {
+  bool neg = false;
+  if (s < e && (*s == '+' || *s == '-')) {
+    neg = *s == '-';
+    ++s;
+  }
+  if (s >= e || *s < '0' || *s > '9') return false;
+  unsigned long long x = 0;
+  bool ovf = false;
+  for (; s < e && *s >= '0' && *s <= '9'; ++s) {
+    const unsigned d = (unsigned)(*s - '0');
+    if (x > (ULLONG_MAX - d) / 10) ovf = true;
+    else x = x * 10 + d;
+  }
+  if (neg) *out = (ovf || x > (unsigned long long)LLONG_MAX + 1) ? LLONG_MIN : (long long)(0 - x);
+  else *out = (ovf || x > (unsigned long long)LLONG_MAX) ? LLONG_MAX : (long long)x;
+  return true;
+}
+
+// strtod on a token: std::from_chars (correctly rounded, as glibc's strtod)
+// when it takes the whole token and gives a number; anything else (a leading
+// '+', hex, out of range, NaN, trailing characters) goes through strtod on a
+// copy, so the value is always strtod's
+inline bool parse_double(const char *tb, size_t tl, double *out) {
+  double v;
+  const auto r = std::from_chars(tb, tb + tl, v);
+  if (r.ec == std::errc() && r.ptr == tb + tl && !std::isnan(v)) {
+    *out = v;
+    return true;
+  }
+  char buf[128];
+  if (tl >= sizeof(buf)) return false;
+  std::memcpy(buf, tb, tl);
+  buf[tl] = 0;
+  char *e = nullptr;
+  *out = std::strtod(buf, &e);
+  return e != buf;
+}
 
 inline const char *skip_ws(const char *p, const char *end) {
   while (p < end && (*p == ' ' || *p == '\t' || *p == '\r')) ++p;
@@ -52,7 +102,6 @@ inline const char *skip_ws(const char *p, const char *end) {
 // Parse one entry line [p, eol). Returns false on malformed input.
 inline bool parse_entry(const char *p, const char *eol, int nv, bool is_int,
                         int64_t *i, int64_t *j, double *val) {
-  char buf[128];
   const char *q = p;
   auto next_token = [&](const char **tb, size_t *tl) -> bool {
     q = skip_ws(q, eol);
@@ -65,32 +114,69 @@ inline bool parse_entry(const char *p, const char *eol, int nv, bool is_int,
   };
   const char *tb;
   size_t tl;
+  constexpr size_t kMaxToken = 127;  // longer tokens are malformed
   for (int f = 0; f < 2; ++f) {
-    if (!next_token(&tb, &tl) || tl >= sizeof(buf)) return false;
-    std::memcpy(buf, tb, tl);
-    buf[tl] = 0;
-    char *e = nullptr;
-    const long long x = std::strtoll(buf, &e, 10);
-    if (e == buf) return false;
+    long long x;
+    if (!next_token(&tb, &tl) || tl > kMaxToken || !parse_ll(tb, tb + tl, &x)) return false;
     (f == 0 ? *i : *j) = x;
   }
   if (nv == 0) {
     *val = 1.0;
     return true;
   }
-  if (!next_token(&tb, &tl) || tl >= sizeof(buf)) return false;
-  std::memcpy(buf, tb, tl);
-  buf[tl] = 0;
-  char *e = nullptr;
+  if (!next_token(&tb, &tl) || tl > kMaxToken) return false;
   if (is_int) {
-    const long long x = std::strtoll(buf, &e, 10);
-    if (e == buf) return false;
+    long long x;
+    if (!parse_ll(tb, tb + tl, &x)) return false;
     *val = (double)(int)x;
-  } else {
-    *val = std::strtod(buf, &e);
-    if (e == buf) return false;
+    return true;
   }
-  return true;  // a complex file's imaginary part is ignored
+  return parse_double(tb, tl, val);  // a complex file's imaginary part is ignored
+}
+
+// Reads a whole file into a NUL-terminated buffer, in parallel pieces.
+bool read_file(const char *path, std::unique_ptr<char[]> *buf, size_t *size) {
+  const int fd = ::open(path, O_RDONLY);
+  if (fd < 0) return false;
+  struct stat st;
+  if (::fstat(fd, &st) != 0 || st.st_size < 0) {
+    ::close(fd);
+    return false;
+  }
+  const size_t n = (size_t)st.st_size;
+  buf->reset(new (std::nothrow) char[n + 1]);
+  if (!*buf) {
+    ::close(fd);
+    return false;
+  }
+  char *b = buf->get();
+  b[n] = 0;
+  unsigned nthr = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+  if (n < (64u << 20)) nthr = 1;
+  std::vector<int> ok(nthr, 1);
+  auto piece = [&](unsigned k) {
+    size_t a = n * k / nthr;
+    const size_t e = n * (k + 1) / nthr;
+    while (a < e) {
+      const ssize_t r = ::pread(fd, b + a, e - a, (off_t)a);
+      if (r <= 0) {
+        if (r < 0 && errno == EINTR) continue;
+        ok[k] = 0;
+        return;
+      }
+      a += (size_t)r;
+    }
+  };
+  if (nthr == 1) {
+    piece(0);
+  } else {
+    std::vector<std::thread> th;
+    for (unsigned k = 0; k < nthr; ++k) th.emplace_back(piece, k);
+    for (auto &t : th) t.join();
+  }
+  ::close(fd);
+  *size = n;
+  return std::all_of(ok.begin(), ok.end(), [](int v) { return v != 0; });
 }
 
 // Equal-nnz row split (see the header).
@@ -131,23 +217,14 @@ pf_status pf_mmio_read(const char *path, int64_t *m_out, int64_t *n_out,
     pf::set_error("pf_mmio_read: null argument");
     return PF_ERR_INVALID;
   }
-  FILE *f = std::fopen(path, "rb");
-  if (!f) {
-    pf::set_error("pf_mmio_read: cannot open %s: %s", path, std::strerror(errno));
+  std::unique_ptr<char[]> text;
+  size_t text_size = 0;
+  if (!read_file(path, &text, &text_size)) {
+    pf::set_error("pf_mmio_read: cannot read %s: %s", path, std::strerror(errno));
     return PF_ERR_IO;
   }
-  std::fseek(f, 0, SEEK_END);
-  const long fsz = std::ftell(f);
-  std::fseek(f, 0, SEEK_SET);
-  std::string text((size_t)std::max(0L, fsz), '\0');
-  const size_t got = fsz > 0 ? std::fread(&text[0], 1, (size_t)fsz, f) : 0;
-  std::fclose(f);
-  if ((long)got != fsz) {
-    pf::set_error("pf_mmio_read: short read on %s", path);
-    return PF_ERR_IO;
-  }
-  const char *p = text.data();
-  const char *end = p + text.size();
+  const char *p = text.get();
+  const char *end = p + text_size;
   auto line_end = [&](const char *s) {
     const char *e = (const char *)std::memchr(s, '\n', (size_t)(end - s));
     return e ? e : end;
@@ -243,9 +320,13 @@ pf_status pf_mmio_read(const char *path, int64_t *m_out, int64_t *n_out,
     return PF_ERR_FORMAT;
   }
   Entries E;
-  E.ri.resize((size_t)NZ);
-  E.ci.resize((size_t)NZ);
-  E.v.resize((size_t)NZ);
+  E.ri.reset(new (std::nothrow) int32_t[(size_t)std::max<long long>(NZ, 1)]);
+  E.ci.reset(new (std::nothrow) int32_t[(size_t)std::max<long long>(NZ, 1)]);
+  E.v.reset(new (std::nothrow) double[(size_t)std::max<long long>(NZ, 1)]);
+  if (!E.ri || !E.ci || !E.v) {
+    pf::set_error("pf_mmio_read: out of host memory");
+    return PF_ERR_INVALID;
+  }
   std::vector<int> bad(nthr, 0);
   {
     std::vector<std::thread> th;
@@ -282,17 +363,36 @@ pf_status pf_mmio_read(const char *path, int64_t *m_out, int64_t *n_out,
     pf::set_error("pf_mmio_read: symmetric file with M != N");
     return PF_ERR_FORMAT;
   }
+  text.reset();
 
-  // counting sort in file order
+  // counting sort in file order: row counts (threads add atomically), then
+  // each thread owns an equal-nnz range of rows and walks all entries in file
+  // order, placing the ones (and the mirrors) that land in its rows, so every
+  // row receives its entries in the same order as a single pass would give
   int64_t *rp = (int64_t *)std::calloc((size_t)M + 1, sizeof(int64_t));
   if (!rp) {
     pf::set_error("pf_mmio_read: out of host memory");
     return PF_ERR_INVALID;
   }
-  for (int64_t k = 0; k < NZ; ++k) {
-    rp[E.ri[(size_t)k]]++;
-    if (sym && E.ri[(size_t)k] != E.ci[(size_t)k]) rp[E.ci[(size_t)k]]++;
-  }
+  unsigned ncsr = std::max(1u, std::min(64u, std::thread::hardware_concurrency()));
+  if (NZ < (1 << 20)) ncsr = 1;
+  auto parallel = [&](auto &&fn) {
+    if (ncsr == 1) {
+      fn(0u);
+      return;
+    }
+    std::vector<std::thread> th;
+    for (unsigned k = 0; k < ncsr; ++k) th.emplace_back(fn, k);
+    for (auto &t : th) t.join();
+  };
+  parallel([&](unsigned k) {
+    const int64_t a = NZ * (int64_t)k / ncsr, b = NZ * (int64_t)(k + 1) / ncsr;
+    for (int64_t q = a; q < b; ++q) {
+      const int32_t i = E.ri[(size_t)q], j = E.ci[(size_t)q];
+      __atomic_fetch_add(&rp[i], 1, __ATOMIC_RELAXED);
+      if (sym && i != j) __atomic_fetch_add(&rp[j], 1, __ATOMIC_RELAXED);
+    }
+  });
   int64_t run = 0;
   for (int64_t r = 0; r <= M; ++r) {
     const int64_t c = rp[r];
@@ -302,7 +402,6 @@ pf_status pf_mmio_read(const char *path, int64_t *m_out, int64_t *n_out,
   const int64_t nnz = run;
   int32_t *col = (int32_t *)std::malloc(sizeof(int32_t) * (size_t)std::max<int64_t>(nnz, 1));
   double *val = (double *)std::malloc(sizeof(double) * (size_t)std::max<int64_t>(nnz, 1));
-  std::vector<int64_t> cur(rp, rp + M);
   if (!col || !val) {
     std::free(rp);
     std::free(col);
@@ -310,18 +409,30 @@ pf_status pf_mmio_read(const char *path, int64_t *m_out, int64_t *n_out,
     pf::set_error("pf_mmio_read: out of host memory");
     return PF_ERR_INVALID;
   }
-  for (int64_t k = 0; k < NZ; ++k) {
-    const int32_t i = E.ri[(size_t)k], j = E.ci[(size_t)k];
-    const double v = E.v[(size_t)k];
-    int64_t o = cur[(size_t)i]++;
-    col[o] = j;
-    val[o] = v;
-    if (sym && i != j) {
-      o = cur[(size_t)j]++;
-      col[o] = i;
-      val[o] = v;
+  // row ranges of equal nnz (thread k owns rows [rb[k], rb[k + 1]))
+  std::vector<int64_t> rb(ncsr + 1);
+  shard_bounds(rp, M, (int)ncsr, rb.data());
+  parallel([&](unsigned k) {
+    const int32_t r0 = (int32_t)rb[k], r1 = (int32_t)rb[k + 1];
+    if (r0 >= r1) return;
+    std::vector<int64_t> cur(rp + r0, rp + r1);  // next slot of each owned row
+    for (int64_t q = 0; q < NZ; ++q) {
+      const int32_t i = E.ri[(size_t)q];
+      const bool mine = i >= r0 && i < r1;
+      if (!sym && !mine) continue;
+      const int32_t j = E.ci[(size_t)q];
+      if (mine) {
+        const int64_t o = cur[(size_t)(i - r0)]++;
+        col[o] = j;
+        val[o] = E.v[(size_t)q];
+      }
+      if (sym && i != j && j >= r0 && j < r1) {
+        const int64_t o = cur[(size_t)(j - r0)]++;
+        col[o] = i;
+        val[o] = E.v[(size_t)q];
+      }
     }
-  }
+  });
   *m_out = M;
   *n_out = N;
   *nnz_out = nnz;

@@ -58,6 +58,78 @@ def test_matches_live_reference(pf, oracle, tmp_path, field, symmetry, size):
     assert np.array_equal(ours[6], ref[6])
 
 
+REF_PRESENT = os.path.exists(os.path.join(os.path.dirname(HERE), "oracle", "_ref", "libref.so"))
+
+
+@pytest.mark.skipif(not REF_PRESENT, reason="reference build absent")
+@pytest.mark.parametrize("symmetry", ["general", "symmetric"])
+def test_parallel_csr_build_matches_live_reference(pf, oracle, tmp_path, symmetry):
+    """More than 2^20 entries: the CSR is built by several threads, each owning
+    a range of rows. Many repeated coordinates (a 700 x 700 matrix), so the
+    order of entries inside a row (file order, mirrors right after their
+    entry) decides the result."""
+    rng = np.random.default_rng(5)
+    z = (1 << 20) + 12345
+    rows = rng.integers(1, 701, z)
+    cols = rng.integers(1, 701, z)
+    if symmetry == "symmetric":
+        rows, cols = np.maximum(rows, cols), np.minimum(rows, cols)
+    vals = rng.standard_normal(z)
+    p = str(tmp_path / "big.mtx")
+    with open(p, "w") as f:
+        f.write(f"%%MatrixMarket matrix coordinate real {symmetry}\n700 700 {z}\n")
+        f.write("".join(f"{i} {j} {v:.17g}\n" for i, j, v in
+                        zip(rows.tolist(), cols.tolist(), vals.tolist())))
+    ours = pf.mmio_read(p)
+    ref = oracle.ref_mmio(p)
+    assert ours[:4] == ref[:4]
+    assert np.array_equal(ours[4], ref[4].astype(np.int64))
+    assert np.array_equal(ours[5], ref[5])
+    assert np.array_equal(ours[6].view(np.uint64), ref[6].view(np.uint64))
+
+
+@pytest.mark.skipif(not REF_PRESENT, reason="reference build absent")
+def test_value_tokens_match_live_reference(pf, oracle, tmp_path):
+    """Value spellings that take the strtod path (a leading '+', hex, out of
+    range, inf/nan, subnormals) and ones that do not: the same bits as the
+    reference's fscanf %lg."""
+    toks = ["1.5", "+2.25", "-0.0", "1e400", "-1e400", "4.9e-324", "2.2250738585072011e-308",
+            "0x1.8p1", "nan", "-inf", "INF", "1.0E+05", "0.1", "123456789012345678901234567890",
+            "-7", "3.", ".5e-3", "1e-400"]
+    lines = [f"{k + 1}\t {k % 3 + 1}   {t}  " for k, t in enumerate(toks)]
+    lines.append(f"+{len(toks) + 1} +2 6.25")
+    p = tmp_path / "tokens.mtx"
+    p.write_text(f"%%MatrixMarket matrix coordinate real general\n{len(lines)} 3 {len(lines)}\n"
+                 + "\n".join(lines) + "\n")
+    ours = pf.mmio_read(str(p))
+    ref = oracle.ref_mmio(str(p))
+    assert ours[:4] == ref[:4]
+    assert np.array_equal(ours[4], ref[4].astype(np.int64))
+    assert np.array_equal(ours[5], ref[5])
+    assert np.array_equal(ours[6].view(np.uint64), ref[6].view(np.uint64))
+
+
+def test_returned_arrays_own_their_memory(pf, tmp_path):
+    """The CSR arrays are the library's own buffers, handed over without a
+    copy: views of them stay valid after the tuple is dropped, and each buffer
+    goes back to the library once nothing views it."""
+    import gc
+    rng = np.random.default_rng(9)
+    p = str(tmp_path / "own.mtx")
+    write_random_mtx(p, rng, 300, 300, 5000)
+    first = pf.mmio_read(p)
+    expect = [a.copy() for a in first[4:]]
+    views = [a[1:] for a in first[4:]]
+    del first
+    gc.collect()
+    for _ in range(3):
+        pf.mmio_read(p)  # allocations that would reuse freed buffers
+    for v, e in zip(views, expect):
+        assert np.array_equal(v, e[1:])
+    del views
+    gc.collect()
+
+
 @pytest.mark.parametrize("text,status", [
     ("%%MatrixMarket matrix array real general\n2 2\n1\n2\n3\n4\n", 6),
     ("not a banner\n", 6),
