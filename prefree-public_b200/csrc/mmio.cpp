@@ -135,19 +135,21 @@ inline bool parse_entry(const char *p, const char *eol, int nv, bool is_int,
 }
 
 // Reads a whole file into a NUL-terminated buffer, in parallel pieces.
-bool read_file(const char *path, std::unique_ptr<char[]> *buf, size_t *size) {
+// 0: done; 1: the file cannot be opened; 2: it cannot be read (errno says why).
+int read_file(const char *path, std::unique_ptr<char[]> *buf, size_t *size) {
   const int fd = ::open(path, O_RDONLY);
-  if (fd < 0) return false;
+  if (fd < 0) return 1;
   struct stat st;
   if (::fstat(fd, &st) != 0 || st.st_size < 0) {
     ::close(fd);
-    return false;
+    return 2;
   }
   const size_t n = (size_t)st.st_size;
   buf->reset(new (std::nothrow) char[n + 1]);
   if (!*buf) {
     ::close(fd);
-    return false;
+    errno = ENOMEM;
+    return 2;
   }
   char *b = buf->get();
   b[n] = 0;
@@ -176,7 +178,7 @@ bool read_file(const char *path, std::unique_ptr<char[]> *buf, size_t *size) {
   }
   ::close(fd);
   *size = n;
-  return std::all_of(ok.begin(), ok.end(), [](int v) { return v != 0; });
+  return std::all_of(ok.begin(), ok.end(), [](int v) { return v != 0; }) ? 0 : 2;
 }
 
 // Equal-nnz row split (see the header).
@@ -219,8 +221,10 @@ pf_status pf_mmio_read(const char *path, int64_t *m_out, int64_t *n_out,
   }
   std::unique_ptr<char[]> text;
   size_t text_size = 0;
-  if (!read_file(path, &text, &text_size)) {
-    pf::set_error("pf_mmio_read: cannot read %s: %s", path, std::strerror(errno));
+  const int rf = read_file(path, &text, &text_size);
+  if (rf != 0) {
+    pf::set_error("pf_mmio_read: cannot %s %s: %s", rf == 1 ? "open" : "read", path,
+                  std::strerror(errno));
     return PF_ERR_IO;
   }
   const char *p = text.get();
