@@ -94,6 +94,11 @@ inline bool parse_double(const char *tb, size_t tl, double *out) {
   return e != buf;
 }
 
+// the C locale's isspace, inline (the parse calls it for every character)
+inline bool is_space(char c) {
+  return c == ' ' || c == '\t' || c == '\n' || c == '\v' || c == '\f' || c == '\r';
+}
+
 inline const char *skip_ws(const char *p, const char *end) {
   while (p < end && (*p == ' ' || *p == '\t' || *p == '\r')) ++p;
   return p;
@@ -107,7 +112,7 @@ inline bool parse_entry(const char *p, const char *eol, int nv, bool is_int,
     q = skip_ws(q, eol);
     if (q >= eol) return false;
     const char *s = q;
-    while (q < eol && !std::isspace((unsigned char)*q)) ++q;
+    while (q < eol && !is_space(*q)) ++q;
     *tb = s;
     *tl = (size_t)(q - s);
     return true;
