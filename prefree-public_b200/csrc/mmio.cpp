@@ -139,6 +139,45 @@ inline bool parse_entry(const char *p, const char *eol, int nv, bool is_int,
   return parse_double(tb, tl, val);  // a complex file's imaginary part is ignored
 }
 
+// Host threads for a pass over `bytes` bytes (one below 64 MB).
+unsigned host_threads(size_t bytes) {
+  if (bytes < ((size_t)64 << 20)) return 1;
+  return std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+}
+
+// Runs fn(k) for k in [0, nthr) on nthr threads (inline when nthr is 1).
+template <typename F>
+void run_threads(unsigned nthr, F &&fn) {
+  if (nthr <= 1) {
+    fn(0u);
+    return;
+  }
+  std::vector<std::thread> th;
+  for (unsigned k = 0; k < nthr; ++k) th.emplace_back(fn, k);
+  for (auto &t : th) t.join();
+}
+
+// Reads n bytes at file offset off into dst, in parallel pieces; false on a
+// short read or an error (errno says which).
+bool pread_all(int fd, char *dst, size_t n, size_t off) {
+  const unsigned nthr = host_threads(n);
+  std::vector<int> ok(nthr, 1);
+  run_threads(nthr, [&](unsigned k) {
+    size_t a = n * k / nthr;
+    const size_t e = n * (k + 1) / nthr;
+    while (a < e) {
+      const ssize_t r = ::pread(fd, dst + a, e - a, (off_t)(off + a));
+      if (r <= 0) {
+        if (r < 0 && errno == EINTR) continue;
+        ok[k] = 0;
+        return;
+      }
+      a += (size_t)r;
+    }
+  });
+  return std::all_of(ok.begin(), ok.end(), [](int v) { return v != 0; });
+}
+
 // Reads a whole file into a NUL-terminated buffer, in parallel pieces.
 // 0: done; 1: the file cannot be opened; 2: it cannot be read (errno says why).
 int read_file(const char *path, std::unique_ptr<char[]> *buf, size_t *size) {
@@ -158,32 +197,10 @@ int read_file(const char *path, std::unique_ptr<char[]> *buf, size_t *size) {
   }
   char *b = buf->get();
   b[n] = 0;
-  unsigned nthr = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
-  if (n < (64u << 20)) nthr = 1;
-  std::vector<int> ok(nthr, 1);
-  auto piece = [&](unsigned k) {
-    size_t a = n * k / nthr;
-    const size_t e = n * (k + 1) / nthr;
-    while (a < e) {
-      const ssize_t r = ::pread(fd, b + a, e - a, (off_t)a);
-      if (r <= 0) {
-        if (r < 0 && errno == EINTR) continue;
-        ok[k] = 0;
-        return;
-      }
-      a += (size_t)r;
-    }
-  };
-  if (nthr == 1) {
-    piece(0);
-  } else {
-    std::vector<std::thread> th;
-    for (unsigned k = 0; k < nthr; ++k) th.emplace_back(piece, k);
-    for (auto &t : th) t.join();
-  }
+  const bool ok = pread_all(fd, b, n, 0);
   ::close(fd);
   *size = n;
-  return std::all_of(ok.begin(), ok.end(), [](int v) { return v != 0; }) ? 0 : 2;
+  return ok ? 0 : 2;
 }
 
 // Equal-nnz row split (see the header).
@@ -385,15 +402,7 @@ pf_status pf_mmio_read(const char *path, int64_t *m_out, int64_t *n_out,
   }
   unsigned ncsr = std::max(1u, std::min(64u, std::thread::hardware_concurrency()));
   if (NZ < (1 << 20)) ncsr = 1;
-  auto parallel = [&](auto &&fn) {
-    if (ncsr == 1) {
-      fn(0u);
-      return;
-    }
-    std::vector<std::thread> th;
-    for (unsigned k = 0; k < ncsr; ++k) th.emplace_back(fn, k);
-    for (auto &t : th) t.join();
-  };
+  auto parallel = [&](auto &&fn) { run_threads(ncsr, fn); };
   parallel([&](unsigned k) {
     const int64_t a = NZ * (int64_t)k / ncsr, b = NZ * (int64_t)(k + 1) / ncsr;
     for (int64_t q = a; q < b; ++q) {
@@ -511,36 +520,55 @@ static pf_status csr_write(const char *path, int64_t m, int64_t n, int64_t nnz, 
 static pf_status csr_read(const char *path, int64_t want_size, int64_t want_mtime, int64_t *m_out,
                           int64_t *n_out, int64_t *nnz_out, int *sym_out, int64_t **rp_out,
                           int32_t **col_out, double **val_out) {
-  FILE *f = std::fopen(path, "rb");
-  if (!f) {
+  const int fd = ::open(path, O_RDONLY);
+  if (fd < 0) {
     pf::set_error("pf_csr_read: cannot open %s: %s", path, std::strerror(errno));
     return PF_ERR_IO;
   }
   CsrHeader hd;
   int64_t fsize = -1, fmt = 0;
   file_stamp(path, &fsize, &fmt);
-  if (std::fread(&hd, sizeof(hd), 1, f) != 1 || std::memcmp(hd.magic, kCsrMagic, 8) != 0 ||
+  if (!pread_all(fd, (char *)&hd, sizeof(hd), 0) || std::memcmp(hd.magic, kCsrMagic, 8) != 0 ||
       hd.m < 0 || hd.n < 0 || hd.nnz < 0 || hd.m >= ((int64_t)1 << 40) ||
       hd.nnz >= ((int64_t)1 << 40) ||
       fsize != (int64_t)sizeof(hd) + 8 * (hd.m + 1) + 12 * hd.nnz ||
       (want_size >= 0 && (hd.src_size != want_size || hd.src_mtime_ns != want_mtime))) {
-    std::fclose(f);
+    ::close(fd);
     pf::set_error("pf_csr_read: %s is not a matching CSR cache file", path);
     return PF_ERR_FORMAT;
   }
   int64_t *rp = (int64_t *)std::malloc(sizeof(int64_t) * (size_t)(hd.m + 1));
   int32_t *col = (int32_t *)std::malloc(sizeof(int32_t) * (size_t)std::max<int64_t>(hd.nnz, 1));
   double *val = (double *)std::malloc(sizeof(double) * (size_t)std::max<int64_t>(hd.nnz, 1));
-  bool ok = rp && col && val &&
-            std::fread(rp, sizeof(int64_t), (size_t)hd.m + 1, f) == (size_t)hd.m + 1 &&
+  const size_t rp_bytes = sizeof(int64_t) * (size_t)(hd.m + 1);
+  const size_t col_bytes = sizeof(int32_t) * (size_t)hd.nnz;
+  bool ok = rp && col && val && pread_all(fd, (char *)rp, rp_bytes, sizeof(hd)) &&
             (hd.nnz == 0 ||
-             (std::fread(col, sizeof(int32_t), (size_t)hd.nnz, f) == (size_t)hd.nnz &&
-              std::fread(val, sizeof(double), (size_t)hd.nnz, f) == (size_t)hd.nnz));
-  std::fclose(f);
+             (pread_all(fd, (char *)col, col_bytes, sizeof(hd) + rp_bytes) &&
+              pread_all(fd, (char *)val, sizeof(double) * (size_t)hd.nnz,
+                        sizeof(hd) + rp_bytes + col_bytes)));
+  ::close(fd);
   // the CSR must be consistent before anyone indexes with it
   if (ok) ok = rp[0] == 0 && rp[hd.m] == hd.nnz;
-  for (int64_t r = 0; ok && r < hd.m; ++r) ok = rp[r] <= rp[r + 1];
-  for (int64_t k = 0; ok && k < hd.nnz; ++k) ok = col[k] >= 0 && (int64_t)col[k] < hd.n;
+  if (ok) {
+    const unsigned nthr = host_threads(col_bytes + rp_bytes);
+    std::vector<int> good(nthr, 1);
+    run_threads(nthr, [&](unsigned t) {
+      const int64_t r0 = hd.m * (int64_t)t / nthr, r1 = hd.m * (int64_t)(t + 1) / nthr;
+      for (int64_t r = r0; r < r1; ++r)
+        if (rp[r] > rp[r + 1]) {
+          good[t] = 0;
+          return;
+        }
+      const int64_t k0 = hd.nnz * (int64_t)t / nthr, k1 = hd.nnz * (int64_t)(t + 1) / nthr;
+      for (int64_t k = k0; k < k1; ++k)
+        if (col[k] < 0 || (int64_t)col[k] >= hd.n) {
+          good[t] = 0;
+          return;
+        }
+    });
+    ok = std::all_of(good.begin(), good.end(), [](int v) { return v != 0; });
+  }
   if (!ok) {
     std::free(rp);
     std::free(col);
