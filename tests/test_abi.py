@@ -105,3 +105,50 @@ def test_shard_bounds_equal_nnz(pf):
     # every boundary is the first row whose start reaches k * nnz / parts
     for k in range(1, 3):
         assert b[k] == int(np.searchsorted(rp, k * 20 // 3))
+
+
+def _build_and_run(tmp_path, pf, src_name, source, compiler, flags):
+    src = tmp_path / src_name
+    src.write_text(source)
+    exe = tmp_path / (src_name + ".out")
+    lib_dir = os.path.dirname(pf.LIB_PATH)
+    cuda_lib = "/usr/local/cuda/lib64"
+    cmd = [compiler, *flags, "-I", os.path.join(ROOT, "include"), str(src), pf.LIB_PATH,
+           f"-Wl,-rpath,{lib_dir}", f"-Wl,-rpath-link,{cuda_lib}", "-o", str(exe)]
+    subprocess.run(cmd, check=True, capture_output=True, text=True)
+    return subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout
+
+
+def test_c_header_compiles_as_c99_and_links(pf, tmp_path):
+    """A C caller (or an FFI generator reading the header as C) sees every
+    entry point: the header compiles as strict C99 with warnings as errors,
+    each declared function links against the library, and a host-only call
+    runs without a GPU."""
+    names = declared_c_functions()
+    body = ",\n  ".join(f"(fn){n}" for n in names)
+    source = (
+        "#include <stdio.h>\n#include \"prefree_b200.h\"\n"
+        "typedef void (*fn)(void);\n"
+        f"static const fn all[] = {{\n  {body}\n}};\n"
+        "int main(void) {\n"
+        "  printf(\"%s %u\\n\", pf_version(), (unsigned)(sizeof(all) / sizeof(all[0])));\n"
+        "  return 0;\n}\n")
+    out = _build_and_run(tmp_path, pf, "abi_c.c", source, "gcc",
+                         ["-std=c99", "-Wall", "-Wextra", "-Werror", "-Wno-cast-function-type"])
+    assert "sm_100a" in out
+    assert out.split()[-1] == str(len(names))
+
+
+def test_cxx_drop_in_header_links(pf, tmp_path):
+    """The C++ harness's view: include/PreFree.h declares the reference's
+    preFreeSpMV, which resolves against the library (same mangled name)."""
+    source = (
+        "#include <cstdio>\n#include \"PreFree.h\"\n#include \"prefree_b200.h\"\n"
+        "int main() {\n"
+        "  void (*f)(double *, int *, int *, double *, double *, int, int, int, double *,\n"
+        "            double *) = &preFreeSpMV;\n"
+        "  std::printf(\"%s %d\\n\", pf_version(), f != nullptr);\n"
+        "  return 0;\n}\n")
+    out = _build_and_run(tmp_path, pf, "abi_cxx.cpp", source, "g++",
+                         ["-std=c++17", "-Wall", "-Wextra", "-Werror"])
+    assert "sm_100a" in out and out.split()[-1] == "1"
