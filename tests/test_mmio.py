@@ -109,6 +109,28 @@ def test_value_tokens_match_live_reference(pf, oracle, tmp_path):
     assert np.array_equal(ours[6].view(np.uint64), ref[6].view(np.uint64))
 
 
+@pytest.mark.skipif(not REF_PRESENT, reason="reference build absent")
+def test_crlf_and_blank_lines_match_live_reference(pf, oracle, tmp_path):
+    """Windows line endings and blank lines between entries (fscanf skips
+    both): the same CSR as the reference, bit for bit."""
+    rng = np.random.default_rng(3)
+    lines = ["%%MatrixMarket matrix coordinate real symmetric", "% comment", "50 50 300"]
+    for k in range(300):
+        i = int(rng.integers(1, 51))
+        j = int(rng.integers(1, i + 1))
+        lines.append(f"{i} {j} {rng.standard_normal():.17g}")
+        if k % 50 == 7:
+            lines.append("")
+    p = tmp_path / "crlf.mtx"
+    p.write_bytes(("\r\n".join(lines) + "\r\n").encode())
+    ours = pf.mmio_read(str(p))
+    ref = oracle.ref_mmio(str(p))
+    assert ours[:4] == ref[:4]
+    assert np.array_equal(ours[4], ref[4].astype(np.int64))
+    assert np.array_equal(ours[5], ref[5])
+    assert np.array_equal(ours[6].view(np.uint64), ref[6].view(np.uint64))
+
+
 def test_returned_arrays_own_their_memory(pf, tmp_path):
     """The CSR arrays are the library's own buffers, handed over without a
     copy: views of them stay valid after the tuple is dropped, and each buffer
