@@ -65,3 +65,42 @@ def case(name, seed=0):
 
 CASES = ["tiny", "empty_matrix", "one_long_row", "row0_long", "empty_edges", "powerlaw",
          "uniform16", "mixed_long", "unsorted"]
+
+
+def gen_config_host(pf, spec, threads=None):
+    """A whole generated config on the host: (row_ptr int64, col, val, x).
+    Row ranges are generated on several threads straight into the final
+    arrays (the library call releases the GIL); the result equals one call
+    over all rows."""
+    import ctypes as C
+    import os
+    import threading
+    threads = threads or os.cpu_count() or 1
+    s = spec.resolved()
+    m = s.m
+    cuts = [m * k // threads for k in range(threads + 1)]
+    offs = [pf.gen_count(spec, 0, c) for c in cuts]
+    z = offs[-1]
+    rp = np.empty(m + 1, dtype=np.int64)
+    rp[0] = 0
+    col = np.empty(max(z, 1), dtype=np.int32)
+    val = np.empty(max(z, 1), dtype=np.float64)
+    cs = s.c()
+    err = []
+
+    def work(k):
+        r0, r1 = cuts[k], cuts[k + 1]
+        lrp = np.empty(r1 - r0 + 1, dtype=np.int64)
+        st = pf.lib.pf_gen_rows_host(C.byref(cs), r0, r1, lrp.ctypes.data,
+                                     col.ctypes.data + 4 * offs[k], val.ctypes.data + 8 * offs[k])
+        if st:
+            err.append(st)
+        rp[r0 + 1:r1 + 1] = lrp[1:] + offs[k]
+
+    ts = [threading.Thread(target=work, args=(k,)) for k in range(threads)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    assert not err, err
+    return rp, col[:z], val[:z], pf.gen_x_host(spec)
