@@ -6,7 +6,8 @@ SHA-256 digests of row_ptr, col, val and x pin the generator, and the digest
 of y = A*x computed by the oracle's restatement of spmv_serial
 (test/test_cdspmv.cpp:4-20) must equal the one the reference computed: the
 same bits, not just within tolerance. Config 3 is also pinned with fp32
-values and x.
+values and x; config 5 (2^31 non-zeros, int64 row_ptr) on two row slices
+over its full x.
 """
 import hashlib
 import json
@@ -39,4 +40,18 @@ def test_config_and_reference_y_checksums(pf, oracle, name):
     for k, v in got.items():
         assert v == g["sha256"][k], f"{name}: generated {k} changed"
     y = oracle.serial(rp, col, vq, xq)
+    assert sha(y) == g["sha256"]["y"], f"{name}: y differs from the reference's"
+
+
+@pytest.mark.parametrize("name", sorted(GOLD.get("slices", {})))
+def test_config5_slices_and_reference_y(pf, oracle, name):
+    g = GOLD["slices"][name]
+    spec = pf.GenSpec(cfg=5, seed=GOLD["seed"])
+    rp, col, val = pf.gen_rows_host(spec, g["r0"], g["r0"] + g["rows"])
+    x = pf.gen_x_host(spec)
+    assert (len(x), int(rp[-1])) == (g["n"], g["nnz"])
+    got = {"row_ptr": sha(rp), "col": sha(col), "val": sha(val), "x": sha(x)}
+    for k, v in got.items():
+        assert v == g["sha256"][k], f"{name}: generated {k} changed"
+    y = oracle.serial(rp, col, val, x)
     assert sha(y) == g["sha256"]["y"], f"{name}: y differs from the reference's"
