@@ -4,10 +4,13 @@ Loaded by tests/, ``__graft_entry__.smoke()`` and bench.py's cpu_baseline /
 ``--impl reference`` arm, as the checker or the timed CPU baseline; the
 product (prefree-public_b200/) never imports it.
 
-Two libraries:
+Three libraries:
   * ``liboracle.so`` — the C restatement in spmv_oracle.c of the reference's
     ``spmv_serial`` (test/test_cdspmv.cpp:4-20) with int32/int64 offsets and
-    fp64/fp32 inputs, plus per-row |a*x| sums and a compensated sum;
+    fp64/fp32 inputs, plus per-row |a*x| sums and a compensated sum; and, in
+    gen_oracle.c, a separately written host copy of the synthetic config
+    generators (inputs for the reference arm without the library under test,
+    and a second implementation the library's generators are pinned to);
   * ``_ref/libref.so`` — the reference's own ``spmv_serial`` and
     ``mmio_allinone`` (utilities/mmio.cpp:1547-1713), compiled from the
     reference sources by oracle/Makefile;
@@ -50,6 +53,15 @@ def _load_oracle():
             g.restype = None
     lib.oracle_coo_to_csr.argtypes = [_i64, _i64, _vp, _vp, _vp, C.c_int, _vp, _vp, _vp, _vp]
     lib.oracle_coo_to_csr.restype = _i64
+    g = [C.c_int, C.c_int, C.c_uint64, _i64, _i64, _i64]
+    lib.oracle_gen_count.argtypes = g + [_i64, _i64]
+    lib.oracle_gen_count.restype = _i64
+    lib.oracle_gen_rows.argtypes = g + [_i64, _i64, _vp, _vp, _vp]
+    lib.oracle_gen_rows.restype = C.c_int
+    lib.oracle_gen_x.argtypes = g + [_i64, _i64, _vp]
+    lib.oracle_gen_x.restype = C.c_int
+    lib.oracle_gen_resolve.argtypes = [C.c_int, C.POINTER(_i64), C.POINTER(_i64), C.POINTER(_i64)]
+    lib.oracle_gen_resolve.restype = C.c_int
     return lib
 
 
@@ -241,6 +253,64 @@ def coo_to_csr(m: int, ri, ci, vi, symmetric: bool):
     z = lib.oracle_coo_to_csr(m, len(ri), _p(ri), _p(ci), _p(vi), int(symmetric), _p(rp),
                               _p(col), _p(val), _p(cur))
     return rp, col[:z], val[:z]
+
+
+def gen_resolve(cfg: int, m: int = 0, n: int = 0, k: int = 0):
+    """(m, n, k) of a config with its defaults filled in."""
+    mm, nn, kk = _i64(m), _i64(n), _i64(k)
+    if lib.oracle_gen_resolve(cfg, C.byref(mm), C.byref(nn), C.byref(kk)):
+        raise ValueError(f"bad config spec {cfg} m={m} n={n} k={k}")
+    return mm.value, nn.value, kk.value
+
+
+def gen_config(cfg: int, seed: int = 12345, value_mode: int = 0, m: int = 0, n: int = 0,
+               k: int = 0, r0: int = 0, r1: int | None = None, threads: int | None = None):
+    """Rows [r0, r1) of a synthetic config and its full x, from the C
+    restatement of the generators: (row_ptr int64 from 0, col int32, val f64,
+    x f64). Row ranges run on parallel host threads (ctypes releases the GIL)
+    straight into the final arrays."""
+    m, n, k = gen_resolve(cfg, m, n, k)
+    r1 = m if r1 is None else r1
+    threads = threads or os.cpu_count() or 1
+    spec = (cfg, value_mode, seed, m, n, k)
+    cuts = [r0 + (r1 - r0) * t // threads for t in range(threads + 1)]
+    offs = [0] * (threads + 1)
+    cnt = [0] * threads
+
+    def count(t):
+        cnt[t] = lib.oracle_gen_count(*spec, cuts[t], cuts[t + 1])
+
+    _run_threads(count, threads)
+    for t in range(threads):
+        offs[t + 1] = offs[t] + cnt[t]
+    z = offs[-1]
+    rp = np.zeros(r1 - r0 + 1, dtype=np.int64)
+    col = np.zeros(max(z, 1), dtype=np.int32)
+    val = np.zeros(max(z, 1), dtype=np.float64)
+    x = np.zeros(n, dtype=np.float64)
+    xc = [n * t // threads for t in range(threads + 1)]
+    rc = [0] * threads
+
+    def fill(t):
+        a, b = cuts[t], cuts[t + 1]
+        lrp = np.zeros(b - a + 1, dtype=np.int64)
+        rc[t] |= lib.oracle_gen_rows(*spec, a, b, _p(lrp), col.ctypes.data + 4 * offs[t],
+                                     val.ctypes.data + 8 * offs[t])
+        rp[a - r0 + 1:b - r0 + 1] = lrp[1:] + offs[t]
+        rc[t] |= lib.oracle_gen_x(*spec, xc[t], xc[t + 1], x.ctypes.data + 8 * xc[t])
+
+    _run_threads(fill, threads)
+    if any(rc):
+        raise RuntimeError("oracle generator failed")
+    return rp, col[:z], val[:z], x
+
+
+def _run_threads(fn, threads: int):
+    ts = [threading.Thread(target=fn, args=(t,)) for t in range(threads)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
 
 
 def tolerance_report(y, y_ref, abs_sum, eps: float, y_comp=None):
