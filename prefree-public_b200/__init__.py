@@ -26,13 +26,16 @@ PF_OK = 0
 STATUS_NAMES = {0: "PF_OK", 1: "PF_ERR_INVALID", 2: "PF_ERR_CUDA", 3: "PF_ERR_DEVICE",
                 4: "PF_ERR_UNSUPPORTED", 5: "PF_ERR_IO", 6: "PF_ERR_FORMAT"}
 (VARIANT_AUTO, VARIANT_NNZSPLIT, VARIANT_ROWGROUP, VARIANT_NNZSPLIT_LDG, VARIANT_ROWVEC,
- VARIANT_ROWVEC_LX, VARIANT_ROWSTREAM, VARIANT_ROWSTREAM_LX, VARIANT_WARPSPLIT) = range(9)
+ VARIANT_ROWVEC_LX, VARIANT_ROWTILE, VARIANT_ROWTILE_LX, VARIANT_WARPSPLIT) = range(9)
+VARIANT_NAMES = ["auto", "nnzsplit", "rowgroup", "nnzsplit_ldg", "rowvec", "rowvec_lx",
+                 "rowtile", "rowtile_lx", "warpsplit"]
 
 # every extern "C" symbol include/*.h declares (checked by the CPU tests)
 EXPORTED = [
     "pf_last_error", "pf_version", "pf_launch_count",
     "pf_handle_create", "pf_handle_destroy", "pf_handle_set_variant",
-    "pf_handle_set_slice", "pf_handle_device_error",
+    "pf_handle_set_slice", "pf_handle_device_error", "pf_handle_choice_i32",
+    "pf_handle_choice_i64",
     "pf_spmv_f64_i32", "pf_spmv_f64_i64", "pf_spmv_f32_i32", "pf_spmv_f32_i64",
     "pf_spmv_host_f64_i32", "pf_spmv_host_f64_i64", "pf_spmv_host_f32_i32",
     "pf_spmv_host_f32_i64",
@@ -80,6 +83,10 @@ def _load():
     lib.pf_handle_set_variant.argtypes = [vp, C.c_int]
     lib.pf_handle_set_slice.argtypes = [vp, i64]
     lib.pf_handle_device_error.argtypes = [vp, C.POINTER(C.c_uint32), C.c_int]
+    for name in ("pf_handle_choice_i32", "pf_handle_choice_i64"):
+        getattr(lib, name).argtypes = [vp, i64, i64, vp, vp, C.POINTER(C.c_int),
+                                       C.POINTER(C.c_int)]
+        getattr(lib, name).restype = st
     for name in ("pf_spmv_f64_i32", "pf_spmv_f64_i64", "pf_spmv_f32_i32", "pf_spmv_f32_i64",
                  "pf_spmv_f16_i32", "pf_spmv_f16_i64", "pf_spmv_bf16_i32", "pf_spmv_bf16_i64",
                  "pf_spmv_host_f64_i32", "pf_spmv_host_f64_i64", "pf_spmv_host_f32_i32",
@@ -178,6 +185,21 @@ class Handle:
         bits = C.c_uint32()
         _check(lib.pf_handle_device_error(self._h, C.byref(bits), int(clear)))
         return int(bits.value)
+
+    def choice(self, m: int, nnz: int, row_ptr, stream=None):
+        """(variant name, lanes per row) this handle runs for the device
+        CSR with this row_ptr (a torch tensor): the forced variant or the
+        selector's cached choice."""
+        import torch
+        if stream is None:
+            stream = torch.cuda.current_stream().cuda_stream
+        elif hasattr(stream, "cuda_stream"):
+            stream = stream.cuda_stream
+        v, ln = C.c_int(), C.c_int()
+        fn = lib.pf_handle_choice_i64 if row_ptr.element_size() == 8 else lib.pf_handle_choice_i32
+        _check(fn(self._h, int(m), int(nnz), row_ptr.data_ptr(), C.c_void_p(stream),
+                  C.byref(v), C.byref(ln)))
+        return VARIANT_NAMES[v.value], int(ln.value)
 
     def close(self):
         if self._h:

@@ -11,7 +11,7 @@
 #include "spmv_nnzsplit.cuh"
 #include "spmv_rowgroup.cuh"
 #include "spmv_rowvec.cuh"
-#include "spmv_rowstream.cuh"
+#include "spmv_rowtile.cuh"
 #include "spmv_tma.cuh"
 #include "spmv_warpsplit.cuh"
 #include "spmm_rowvec.cuh"
@@ -43,7 +43,7 @@ void count_launches(unsigned long long k) { count_launch(k); }
 // The selector's decision for one matrix.
 struct pf_variant_choice {
   int variant;  // a PF_VARIANT_* other than AUTO
-  int lanes;    // lanes per row for the row-group variants (ROWVEC, ROWGROUP, ROWSTREAM)
+  int lanes;    // lanes per row for the row-group variants (ROWVEC, ROWGROUP, ROWTILE)
 };
 
 struct pf_select_entry {
@@ -73,7 +73,7 @@ struct pf_handle_s {
   int64_t cap = 0;
   bool scratch_dirty = false;
   unsigned *err = nullptr;
-  // long-row chunk descriptors (ROWVEC_LX, ROWSTREAM_LX), one allocation,
+  // long-row chunk descriptors (ROWVEC_LX, ROWTILE_LX), one allocation,
   // counters zeroed when grown
   void *lx_buf = nullptr;
   size_t lx_bytes = 0;
@@ -197,10 +197,23 @@ static int rowgroup_lanes(double avg) {
   return v;
 }
 
-// ROWSTREAM lanes: one to two 8-element steps per lane for an average row
-static int rowstream_lanes(double avg) {
+// ROWTILE shape: threads per CTA, non-zeros per window, CTAs per SM; lanes
+// per row (a power of two, NT / lanes rows per tile) so that an average tile
+// fills about one window
+#ifndef PF_RT_NT
+#define PF_RT_NT 128
+#endif
+#ifndef PF_RT_CAP
+#define PF_RT_CAP 1024
+#endif
+#ifndef PF_RT_MINB
+#define PF_RT_MINB 8
+#endif
+constexpr int kRowTileNT = PF_RT_NT;
+constexpr int kRowTileCap = PF_RT_CAP;
+static int rowtile_lanes(double avg) {
   int v = 1;
-  while (v < 32 && 6 * v < avg) v *= 2;
+  while (v < 32 && avg * (kRowTileNT / v) > 0.9 * kRowTileCap) v *= 2;
   return v;
 }
 
@@ -249,8 +262,8 @@ static pf_status select_variant(pf_handle h, int64_t m, int64_t nnz, const IT *r
   if (h->variant != PF_VARIANT_AUTO) {
     const double avg = m > 0 ? (double)nnz / (double)m : 0.0;
     const bool rv = h->variant == PF_VARIANT_ROWVEC || h->variant == PF_VARIANT_ROWVEC_LX;
-    const bool rs = h->variant == PF_VARIANT_ROWSTREAM || h->variant == PF_VARIANT_ROWSTREAM_LX;
-    *out = pf_variant_choice{h->variant, rs ? rowstream_lanes(avg)
+    const bool rt = h->variant == PF_VARIANT_ROWTILE || h->variant == PF_VARIANT_ROWTILE_LX;
+    *out = pf_variant_choice{h->variant, rt ? rowtile_lanes(avg)
                                             : rv ? rowvec_lanes(avg) : rowgroup_lanes(avg)};
     return PF_OK;
   }
@@ -341,39 +354,42 @@ static pf_status launch_rowvec(pf_handle h, const SpmvParams<VT, IT> &prm, bool 
   return PF_OK;
 }
 
-template <typename VT, typename IT, int V>
-static pf_status launch_rowstream(pf_handle h, const SpmvParams<VT, IT> &prm, bool lx,
-                                  cudaStream_t st) {
-  using C = RowStreamCfg;
-  static int occ[kMaxDevices][2] = {};
-  const size_t smem = sizeof(RowStreamSmem<VT, IT>);
-  auto kern = lx ? spmv_rowstream_kernel<VT, IT, V, true> : spmv_rowstream_kernel<VT, IT, V, false>;
-  int &o = occ[h->device % kMaxDevices][lx ? 1 : 0];
-  if (o == 0) {
-    PF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    int v = 0;
-    PF_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kern, C::NTP, smem));
-    o = std::max(1, v);
+// ROWTILE: tiles of NT / VR rows; one wave of resident CTAs striding over
+// the tiles (each prefetches its next tile's row bounds). LX lists rows
+// longer than one window for the chunk kernel.
+template <typename VT, typename IT, int VR>
+static pf_status launch_rowtile(pf_handle h, const SpmvParams<VT, IT> &prm, bool lx,
+                                cudaStream_t st) {
+  constexpr int NT = kRowTileNT, CAP = kRowTileCap, MINB = PF_RT_MINB;
+  constexpr int R = NT / VR;
+  static int occ_dev[kMaxDevices][2] = {};
+  int &occ = occ_dev[h->device % kMaxDevices][lx ? 1 : 0];
+  if (occ == 0) {
+    int o = 0;
+    if (lx)
+      PF_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+          &o, spmv_rowtile_kernel<VT, IT, NT, VR, CAP, true, MINB>, NT, 0));
+    else
+      PF_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+          &o, spmv_rowtile_kernel<VT, IT, NT, VR, CAP, false, MINB>, NT, 0));
+    occ = std::max(1, o);
   }
-  constexpr int GROUPS = C::NT / V;
-  const double avg = (double)prm.nnz / (double)prm.m;
-  int rpg = (int)(0.75 * C::CAP / (std::max(avg, 1.0) * GROUPS));
-  rpg = std::max(1, std::min(rpg, C::RMAX / GROUPS));
-  const int64_t R = (int64_t)GROUPS * rpg;
-  const int64_t ntiles = ceil_div(prm.m, R);
-  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(ntiles, (int64_t)h->num_sms * o));
-  const int lt = 16 * V;                 // longer in-tile rows: one warp each
-  const int64_t lx_lt = 256;             // longer rows of unstaged tiles: chunk kernel
-  if (lx) {
-    pf_status s = ensure_lx(h, prm.nnz, lx_lt, kLxChunk, st);
-    if (s != PF_OK) return s;
-  }
-  kern<<<grid, C::NTP, smem, st>>>(prm, lx ? h->lx : LongRowScratch{}, rpg, lt, lx_lt, kLxChunk);
-  count_launch();
-  if (lx) {
-    launch_chunks<VT, IT>(h, prm, st);
+  const int64_t tiles = ceil_div(prm.m, (int64_t)R);
+  const unsigned grid =
+      (unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)h->num_sms * occ));
+  if (!lx) {
+    spmv_rowtile_kernel<VT, IT, NT, VR, CAP, false, MINB>
+        <<<grid, NT, 0, st>>>(prm, LongRowScratch{}, INT64_MAX, kLxChunk);
     count_launch();
+    PF_CUDA_TRY(cudaGetLastError());
+    return PF_OK;
   }
+  const int64_t lt = CAP;
+  pf_status s = ensure_lx(h, prm.nnz, lt, kLxChunk, st);
+  if (s != PF_OK) return s;
+  spmv_rowtile_kernel<VT, IT, NT, VR, CAP, true, MINB><<<grid, NT, 0, st>>>(prm, h->lx, lt, kLxChunk);
+  launch_chunks<VT, IT>(h, prm, st);
+  count_launch(2);
   PF_CUDA_TRY(cudaGetLastError());
   return PF_OK;
 }
@@ -493,9 +509,6 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
   if (kHalf) {
     // 16-bit values run on the row-vector, warp-slice and plain-load kernels
     const double avg = (double)nnz / (double)m;
-    if (ch.variant == PF_VARIANT_ROWSTREAM) ch = pf_variant_choice{PF_VARIANT_ROWVEC, rowvec_lanes(avg)};
-    if (ch.variant == PF_VARIANT_ROWSTREAM_LX)
-      ch = pf_variant_choice{PF_VARIANT_ROWVEC_LX, rowvec_lanes(avg)};
     if (ch.variant == PF_VARIANT_NNZSPLIT) ch.variant = PF_VARIANT_NNZSPLIT_LDG;
   }
 
@@ -526,24 +539,23 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
     ch.variant = PF_VARIANT_ROWGROUP;
     ch.lanes = rowgroup_lanes(m > 0 ? (double)nnz / (double)m : 0.0);
   }
-  if constexpr (!kHalf) {
-    if (ch.variant == PF_VARIANT_ROWSTREAM || ch.variant == PF_VARIANT_ROWSTREAM_LX) {
-      // the long-row chunk kernel uses 16-byte loads: unaligned col/val keep
-      // long rows of unstaged tiles in the row kernel instead
-      const bool lx = ch.variant == PF_VARIANT_ROWSTREAM_LX &&
-                      (((uintptr_t)col | (uintptr_t)val) & 15) == 0;
-      prm.T = 0;
-      prm.num_ctas = 0;
-      prm.carry_head = prm.carry_tail = nullptr;
-      prm.counters = nullptr;
-      switch (ch.lanes) {
-        case 1: return launch_rowstream<VT, IT, 1>(h, prm, lx, st);
-        case 2: return launch_rowstream<VT, IT, 2>(h, prm, lx, st);
-        case 4: return launch_rowstream<VT, IT, 4>(h, prm, lx, st);
-        case 8: return launch_rowstream<VT, IT, 8>(h, prm, lx, st);
-        case 16: return launch_rowstream<VT, IT, 16>(h, prm, lx, st);
-        default: return launch_rowstream<VT, IT, 32>(h, prm, lx, st);
-      }
+  // ROWTILE_LX's chunk kernel needs 16-byte aligned col/val (16-byte
+  // blocks); ROWTILE itself loads elements
+  if (ch.variant == PF_VARIANT_ROWTILE_LX && (((uintptr_t)col | (uintptr_t)val) & 15) != 0)
+    ch.variant = PF_VARIANT_ROWTILE;
+  if (ch.variant == PF_VARIANT_ROWTILE || ch.variant == PF_VARIANT_ROWTILE_LX) {
+    const bool lx = ch.variant == PF_VARIANT_ROWTILE_LX;
+    prm.T = 0;
+    prm.num_ctas = 0;
+    prm.carry_head = prm.carry_tail = nullptr;
+    prm.counters = nullptr;
+    switch (ch.lanes) {
+      case 1: return launch_rowtile<VT, IT, 1>(h, prm, lx, st);
+      case 2: return launch_rowtile<VT, IT, 2>(h, prm, lx, st);
+      case 4: return launch_rowtile<VT, IT, 4>(h, prm, lx, st);
+      case 8: return launch_rowtile<VT, IT, 8>(h, prm, lx, st);
+      case 16: return launch_rowtile<VT, IT, 16>(h, prm, lx, st);
+      default: return launch_rowtile<VT, IT, 32>(h, prm, lx, st);
     }
   }
   if (ch.variant == PF_VARIANT_ROWVEC || ch.variant == PF_VARIANT_ROWVEC_LX) {
@@ -617,27 +629,13 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
   return PF_OK;
 }
 
-// WARPSPLIT shape: row_ptr window, ring stages, CTAs per SM, non-zeros per
-// lane. The defaults are the best of sweeps on the configs (compile with -D
-// to sweep them).
-#ifndef PF_WS_WIN
-#define PF_WS_WIN 128
-#endif
-#ifndef PF_WS_NS
-#define PF_WS_NS 2
-#endif
-#ifndef PF_WS_MINB
-#define PF_WS_MINB 3
-#endif
-#ifndef PF_WS_EPL
-#define PF_WS_EPL 8
-#endif
-
 // WARPSPLIT: one wave of resident CTAs, one equal-nnz slice per warp (at
 // least one tile each).
 template <typename VT, typename IT>
 static pf_status launch_warpsplit(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st) {
-  constexpr int NTB = 256, WIN = PF_WS_WIN, NS = PF_WS_NS, MINB = PF_WS_MINB, EPL = PF_WS_EPL;
+  // row_ptr window, ring stages, CTAs per SM, non-zeros per lane: the best
+  // of sweeps on the configs
+  constexpr int NTB = 256, WIN = 128, NS = 2, MINB = 3, EPL = 8;
   auto kern = spmv_warpsplit_kernel<VT, IT, NTB, WIN, NS, MINB, EPL>;
   const size_t smem = sizeof(WarpSplitSmem<VT, WIN, NS, EPL>) * (NTB / 32);
   static int occ_dev[kMaxDevices] = {};
@@ -910,6 +908,28 @@ pf_status pf_handle_device_error(pf_handle h, uint32_t *bits, int clear) {
     h->scratch_dirty = true;  // a failed launch may leave counters set
     h->lx_dirty = true;
   }
+  return PF_OK;
+}
+
+pf_status pf_handle_choice_i32(pf_handle h, int64_t m, int64_t nnz, const int32_t *row_ptr,
+                               void *stream, int *variant, int *lanes) {
+  PF_CHECK_ARG(h && variant && lanes && row_ptr && m > 0 && nnz > 0, "bad argument");
+  pf_variant_choice ch;
+  pf_status s = select_variant<int32_t>(h, m, nnz, row_ptr, (cudaStream_t)stream, &ch);
+  if (s != PF_OK) return s;
+  *variant = ch.variant;
+  *lanes = ch.lanes;
+  return PF_OK;
+}
+
+pf_status pf_handle_choice_i64(pf_handle h, int64_t m, int64_t nnz, const int64_t *row_ptr,
+                               void *stream, int *variant, int *lanes) {
+  PF_CHECK_ARG(h && variant && lanes && row_ptr && m > 0 && nnz > 0, "bad argument");
+  pf_variant_choice ch;
+  pf_status s = select_variant<int64_t>(h, m, nnz, row_ptr, (cudaStream_t)stream, &ch);
+  if (s != PF_OK) return s;
+  *variant = ch.variant;
+  *lanes = ch.lanes;
   return PF_OK;
 }
 

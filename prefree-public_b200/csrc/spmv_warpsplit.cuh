@@ -41,11 +41,6 @@
 #include "spmv_nnzsplit.cuh"
 #include "spmv_tma.cuh"
 
-// the fast tile walk (0: every tile takes the searching pass)
-#ifndef PF_WS_FAST
-#define PF_WS_FAST 1
-#endif
-
 namespace pf {
 
 // first j in [0, WIN) with E[j] > key (WIN if none)
@@ -268,7 +263,7 @@ spmv_warpsplit_kernel(const SpmvParams<VT, IT> P) {
     // order as pass(). False (nothing changed) when the tile does not qualify.
     auto fast_tile = [&](int tb, const double(&p)[EPL]) -> bool {
       const int tend = tb + TILE;
-      if (!PF_WS_FAST || tb < 0 || tend > L || g != tb || E[off] <= tb) return false;
+      if (tb < 0 || tend > L || g != tb || E[off] <= tb) return false;
       uint32_t *M = S.ends;
       if (lane < EPL) M[lane] = 0u;
       __syncwarp();
