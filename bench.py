@@ -15,10 +15,18 @@ Timing: W warm-up steps, then K steps between barrier + synchronize, CUDA
 events on the compute stream, max over ranks. Inputs (27 GB) are far larger
 than L2 (126 MB), so no flush is needed between steps.
 
+At N = 1 the line also carries `per_config`: configs 1-4 (and config 3 with
+fp32 values) on one GPU, L2 warm and, for configs 1 and 3, cold; cuSPARSE on
+the same arrays; and the reference's spmv_serial on this host.
+
 `--impl reference` times the reference's own CPU SpMV (spmv_serial of
 test/test_cdspmv.cpp:4-20, compiled from the reference sources into
 oracle/_ref/libref.so) on a bounded row sample of the same workload, with
-every host thread (row slices in parallel); rank 0 only.
+every host thread (row slices in parallel); rank 0 only. Its inputs come from
+the oracle's own generator (oracle/gen_oracle.c), not from the library under
+test. At N = 1 it adds `per_config`: the reference's own GPU path
+(preFreeSpMV compiled for sm_100a) on configs 1-4 with its own cdTime and
+cdPre.
 """
 from __future__ import annotations
 
@@ -118,44 +126,51 @@ def traffic_per_row():
         return json.load(f).get("dram_bytes_per_row")
 
 
-def cpu_reference_sample(pf, oracle, spec, rows: int, threads: int):
-    """Host CSR sample (rows [0, rows)) of the workload + full x, generated on
-    the host (library generator, parallel row ranges)."""
-    s = spec.resolved()
-    x = np.zeros(s.n, dtype=np.float64)
-    rp = np.zeros(rows + 1, dtype=np.int64)
-    z = pf.gen_count(spec, 0, rows)
-    col = np.zeros(z, dtype=np.int32)
-    val = np.zeros(z, dtype=np.float64)
-    cs = s.c()
-    cuts = [rows * k // threads for k in range(threads + 1)]
-    xc = [s.n * k // threads for k in range(threads + 1)]
+PER_CONFIGS = [(1, "f64"), (2, "f64"), (3, "f64"), (3, "f32"), (4, "f64")]
 
-    def work(k):
-        r0, r1 = cuts[k], cuts[k + 1]
-        o0 = pf.gen_count(spec, 0, r0)
-        lrp = np.zeros(r1 - r0 + 1, dtype=np.int64)
-        pf._check(pf.lib.pf_gen_rows_host(C.byref(cs), r0, r1, lrp.ctypes.data,
-                                          col.ctypes.data + 4 * o0, val.ctypes.data + 8 * o0))
-        rp[r0 + 1:r1 + 1] = lrp[1:] + o0
-        pf._check(pf.lib.pf_gen_x_host(C.byref(cs), xc[k], xc[k + 1], x.ctypes.data + 8 * xc[k]))
 
-    ts = [threading.Thread(target=work, args=(k,)) for k in range(threads)]
-    [t.start() for t in ts]
-    [t.join() for t in ts]
-    return rp, col, val, x
+def compulsory_bytes(m, n, nnz, vbytes, ibytes):
+    """nnz*(V+4) + (m+1)*R + n*V + m*V: the reference's data_origin1
+    (test/test_cdspmv.cpp:305) with beta = 0."""
+    return nnz * (vbytes + 4) + (m + 1) * ibytes + n * vbytes + m * vbytes
+
+
+def reference_gpu_per_config(oracle, threads):
+    """The reference's own GPU path (preFreeSpMV compiled unmodified for
+    sm_100a, oracle/_ref/libref_gpu.so) on configs 1-4, fp64 (its only value
+    type): its own cdTime (ms per multiply, 4000 launches after 200 warm-ups,
+    L2 warm, src/spmv_kernel/preFreeSpMV.cu:604-650) and cdPre (its start-row
+    pre-pass), and whether its y meets the tolerance against spmv_serial.
+    Inputs from the oracle's generator."""
+    if not oracle.ref_gpu_available():
+        return {"unavailable": "oracle/_ref/libref_gpu.so not built"}
+    out = {}
+    for cfg in (1, 2, 3, 4):
+        rp, col, val, x = oracle.gen_config(cfg, seed=SEED, threads=threads)
+        m, n, z = len(rp) - 1, len(x), len(col)
+        rp32 = rp.astype(np.int32)
+        y, cd, pre = oracle.ref_gpu_prefree(val, rp32, col, x, m, n)
+        ref = oracle.ref_serial_threaded(rp32, col, val, x, threads)
+        a, comp = oracle.abs_comp(rp, col, val, x)
+        _, _, nbad = oracle.tolerance_report(y, ref, a, 1e-12, y_comp=comp)
+        B = compulsory_bytes(m, n, z, 8, 4)
+        out[f"c{cfg}_f64"] = {"m": m, "nnz": z, "cdTime_us": cd * 1e3, "cdPre_us": pre * 1e3,
+                              "gflops": 2 * z / (cd * 1e6), "alg_GBps": B / (cd * 1e6),
+                              "rows_out_of_tolerance": nbad}
+        del rp, rp32, col, val, x, y, ref, a, comp
+    out["timing"] = "the reference's own cdTime / cdPre (preFreeSpMV.cu:604-650), L2 warm"
+    return out
 
 
 def run_reference(args, rank):
-    """--impl reference: the reference's CPU spmv_serial on all host threads."""
+    """--impl reference: the reference's CPU spmv_serial on all host threads
+    (the headline), plus at N = 1 the reference's own GPU path per config."""
     if rank != 0:
         return
-    pf = importlib.import_module("prefree-public_b200")
     import oracle
     threads = os.cpu_count() or 1
-    spec = pf.GenSpec(cfg=5, seed=SEED)
     rows = 1 << 23                      # 2^28 non-zeros per sampled step
-    rp, col, val, x = cpu_reference_sample(pf, oracle, spec, rows, threads)
+    rp, col, val, x = oracle.gen_config(5, seed=SEED, r0=0, r1=rows, threads=threads)
     rp32 = rp.astype(np.int32)
     kind = "reference" if oracle.ref_available() else "port"
 
@@ -171,19 +186,153 @@ def run_reference(args, rank):
         one()
     dt = (time.perf_counter() - t0) / args.steps
     z = int(rp[-1])
+    del rp, rp32, col, val, x
     v = 2.0 * z / dt / 1e9
     sample = (f"rows [0, 2^23) of config 5 ({z} nnz, x of 2^26) per step; "
               f"spmv_serial on {threads} equal-nnz row slices in parallel threads")
+    per = None
+    if int(os.environ.get("WORLD_SIZE", "1")) == 1 and not args.no_per_config:
+        per = reference_gpu_per_config(oracle, threads)
     print(json.dumps({
         "metric": METRIC, "value": v, "unit": "GFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
-        "data": "synthetic (seeded generator)", "impl": "reference",
+        "data": "synthetic (seeded generator, oracle/gen_oracle.c)", "impl": "reference",
         "config": {"workload": WORKLOAD, "parallelism": "host threads", "sample_rows": rows},
         "cpu_baseline": {"value": v, "unit": "GFLOP/s", "cores": threads, "kind": kind,
                          "sample": sample},
         "e2e": {"value": v, "unit": "GFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "per_config": per,
     }), flush=True)
+
+
+def _median(v):
+    return float(statistics.median(v))
+
+
+def time_graph_us(torch, fn, launches=200, repeats=5):
+    """Per-launch µs of `fn` replayed back to back from one CUDA graph of
+    `launches` calls (L2 warm, like the reference's launch loop): the median
+    of `repeats` replays, CUDA events on the capturing stream."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            fn()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(launches):
+                fn()
+        g.replay()
+        ts = []
+        for _ in range(repeats):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            g.replay()
+            e1.record(s)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3 / launches)
+    torch.cuda.current_stream().wait_stream(s)
+    del g
+    return _median(ts)
+
+
+def time_cold_us(torch, fn, flush, reps=20):
+    """Per-launch µs with L2 flushed before every launch: a write of `flush`
+    (four times the L2 size) outside the timed events; median of `reps`."""
+    st = torch.cuda.current_stream()
+    for _ in range(3):
+        fn()
+    ts = []
+    for i in range(reps):
+        flush.fill_(i & 0xff)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        fn()
+        e1.record(st)
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3)
+    return _median(ts)
+
+
+def per_config_block(pf, torch, dev, with_cpu: bool):
+    """Configs 1-4 (config 3 also with fp32 values) on one GPU, each through
+    the auto-selected variant: per-launch µs (L2 warm: median of 5 replays of
+    200 launches; configs 1 and 3 also cold-L2), algorithmic GB/s and its
+    fraction of the measured copy peak and of 8 TB/s; cuSPARSE CSR SpMV
+    (torch sparse CSR, int32 indices) on the same device arrays; and, when
+    with_cpu, the reference's spmv_serial (one thread, median of 3) on the
+    same matrix on this host."""
+    import oracle
+    hbm_peak, peak_src = peaks()
+    h = pf.Handle()
+    flush = torch.empty(4 * 126 * 2**20 // 4, dtype=torch.int32, device=dev)  # 504 MB
+    out = {}
+    launches0 = pf.launch_count()
+    for cfg, vname in PER_CONFIGS:
+        vdt = {"f64": torch.float64, "f32": torch.float32}[vname]
+        spec = pf.GenSpec(cfg=cfg, seed=SEED).resolved()
+        rp, col, val = pf.gen_rows_device(spec, index_dtype=torch.int32, value_dtype=vdt,
+                                          device=dev)
+        x = pf.gen_x_device(spec, value_dtype=vdt, device=dev)
+        y = torch.empty(spec.m, dtype=vdt, device=dev)
+        z = col.numel()
+
+        def ours():
+            pf.spmv(h, spec.m, spec.n, z, rp, col, val, x, y)
+
+        warm = time_graph_us(torch, ours)
+        cold = time_cold_us(torch, ours, flush) if cfg in (1, 3) else None
+        assert h.device_error() == 0, "device error word set"
+        B = compulsory_bytes(spec.m, spec.n, z, val.element_size(), 4)
+        e = {"m": spec.m, "nnz": z, "variant": "%s/%d" % h.choice(spec.m, z, rp),
+             "alg_bytes": B, "us": warm, "gflops": 2 * z / warm / 1e3,
+             "alg_GBps": B / warm / 1e3, "frac_of_" + peak_src: B / warm / 1e3 / hbm_peak,
+             "frac_of_8TBps": B / warm / 1e3 / 8000.0}
+        if cold is not None:
+            e["cold_l2_us"] = cold
+            e["cold_l2_frac_of_" + peak_src] = B / cold / 1e3 / hbm_peak
+        try:
+            A = torch.sparse_csr_tensor(rp, col, val, size=(spec.m, spec.n))
+            xv = x.unsqueeze(1)
+            yv = torch.empty(spec.m, 1, dtype=vdt, device=dev)
+            e["cusparse_us"] = time_graph_us(torch, lambda: torch.matmul(A, xv, out=yv))
+            del A, xv, yv
+        except RuntimeError as ex:
+            e["cusparse_us"] = None
+            e["cusparse_error"] = str(ex).splitlines()[0][:200]
+        if with_cpu:
+            hrp, hcol = rp.cpu().numpy(), col.cpu().numpy()
+            hval = val.double().cpu().numpy()   # fp32 values widened: spmv_serial is fp64
+            hx = x.double().cpu().numpy()
+            kind = "reference" if oracle.ref_available() else "port"
+            ts = []
+            for _ in range(3):
+                t0 = time.perf_counter()
+                if kind == "reference":
+                    oracle.ref_serial(hrp, hcol, hval, hx)
+                else:
+                    oracle.serial(hrp.astype(np.int64), hcol, hval, hx)
+                ts.append(time.perf_counter() - t0)
+            e["cpu_spmv_serial_ms"] = _median(ts) * 1e3
+            e["cpu_gflops"] = 2 * z / _median(ts) / 1e9
+            e["cpu_kind"] = kind
+            del hrp, hcol, hval, hx
+        out[f"c{cfg}_{vname}"] = e
+        del rp, col, val, x, y
+        torch.cuda.empty_cache()
+    out["launches"] = int(pf.launch_count() - launches0)
+    out["timing"] = ("ours and cuSPARSE: median of 5 replays of a 200-launch CUDA graph, L2 warm "
+                     "(as the reference's 4000-launch loop); cold_l2: L2 flushed by a 504 MB "
+                     "write before each launch, outside the events, median of 20")
+    if with_cpu:
+        out["cpu"] = {"cores": 1, "threads_available": os.cpu_count(),
+                      "what": "the reference's spmv_serial (test/test_cdspmv.cpp:4-20), one "
+                              "thread, median of 3; fp32 values widened to fp64"}
+    h.close()
+    del flush
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_kernel_mode(args):
@@ -276,6 +425,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-per-config", action="store_true",
+                    help="skip the per-config block (configs 1-4 on one GPU)")
     ap.add_argument("--path", default="fused", choices=["fused", "nccl"],
                     help="power mode: fused multiply + all-gather kernel, or SpMV + NCCL")
     ap.add_argument("--barrier", default="kernel", choices=["kernel", "host"],
@@ -483,6 +634,10 @@ def main():
                "sample": f"rows [0, 2^21) of config 5 ({zc} nnz), one multiply, single thread "
                          "(spmv_serial is serial by construction)"}
 
+    per = None
+    if world == 1 and not args.no_per_config:
+        per = per_config_block(pf, torch, dev, with_cpu=not args.no_cpu)
+
     if rank == 0:
         out = {
             "metric": METRIC, "value": 2.0 * z_tot / (step_ms * 1e-3) / 1e9, "unit": "GFLOP/s",
@@ -501,6 +656,7 @@ def main():
             "e2e": e2e,
             "clocks": clocks.summary(),
             "check": {"final_norm_sq_of_y": final_nsq, "final_norm": final_norm},
+            "per_config": per,
         }
         print(json.dumps(out), flush=True)
     h.close()
