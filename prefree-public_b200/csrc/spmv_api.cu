@@ -11,7 +11,6 @@
 #include "spmv_nnzsplit.cuh"
 #include "spmv_rowgroup.cuh"
 #include "spmv_rowvec.cuh"
-#include "spmv_rowtile.cuh"
 #include "spmv_tma.cuh"
 #include "spmv_warpsplit.cuh"
 #include "spmm_rowvec.cuh"
@@ -43,7 +42,7 @@ void count_launches(unsigned long long k) { count_launch(k); }
 // The selector's decision for one matrix.
 struct pf_variant_choice {
   int variant;  // a PF_VARIANT_* other than AUTO
-  int lanes;    // lanes per row for the row-group variants (ROWVEC, ROWGROUP, ROWTILE)
+  int lanes;    // lanes per row for the row-group variants (ROWVEC, ROWGROUP)
 };
 
 struct pf_select_entry {
@@ -73,7 +72,7 @@ struct pf_handle_s {
   int64_t cap = 0;
   bool scratch_dirty = false;
   unsigned *err = nullptr;
-  // long-row chunk descriptors (ROWVEC_LX, ROWTILE_LX), one allocation,
+  // long-row chunk descriptors (ROWVEC_LX), one allocation,
   // counters zeroed when grown
   void *lx_buf = nullptr;
   size_t lx_bytes = 0;
@@ -197,26 +196,6 @@ static int rowgroup_lanes(double avg) {
   return v;
 }
 
-// ROWTILE shape: threads per CTA, non-zeros per window, CTAs per SM; lanes
-// per row (a power of two, NT / lanes rows per tile) so that an average tile
-// fills about one window
-#ifndef PF_RT_NT
-#define PF_RT_NT 128
-#endif
-#ifndef PF_RT_CAP
-#define PF_RT_CAP 1024
-#endif
-#ifndef PF_RT_MINB
-#define PF_RT_MINB 8
-#endif
-constexpr int kRowTileNT = PF_RT_NT;
-constexpr int kRowTileCap = PF_RT_CAP;
-static int rowtile_lanes(double avg) {
-  int v = 1;
-  while (v < 32 && avg * (kRowTileNT / v) > 0.9 * kRowTileCap) v *= 2;
-  return v;
-}
-
 // ROWVEC lanes: one 4-element block per lane covers an average row; long
 // rows use 16 lanes (measured faster than 32 on 2000-non-zero rows: more
 // rows in flight per warp)
@@ -262,9 +241,7 @@ static pf_status select_variant(pf_handle h, int64_t m, int64_t nnz, const IT *r
   if (h->variant != PF_VARIANT_AUTO) {
     const double avg = m > 0 ? (double)nnz / (double)m : 0.0;
     const bool rv = h->variant == PF_VARIANT_ROWVEC || h->variant == PF_VARIANT_ROWVEC_LX;
-    const bool rt = h->variant == PF_VARIANT_ROWTILE || h->variant == PF_VARIANT_ROWTILE_LX;
-    *out = pf_variant_choice{h->variant, rt ? rowtile_lanes(avg)
-                                            : rv ? rowvec_lanes(avg) : rowgroup_lanes(avg)};
+    *out = pf_variant_choice{h->variant, rv ? rowvec_lanes(avg) : rowgroup_lanes(avg)};
     return PF_OK;
   }
   for (int i = 0; i < h->cache_n; ++i) {
@@ -348,46 +325,6 @@ static pf_status launch_rowvec(pf_handle h, const SpmvParams<VT, IT> &prm, bool 
   pf_status s = ensure_lx(h, prm.nnz, lt, kLxChunk, st);
   if (s != PF_OK) return s;
   spmv_rowvec_kernel<VT, IT, V, U, NTB, true, MINB><<<grid, NTB, 0, st>>>(prm, h->lx, lt, kLxChunk);
-  launch_chunks<VT, IT>(h, prm, st);
-  count_launch(2);
-  PF_CUDA_TRY(cudaGetLastError());
-  return PF_OK;
-}
-
-// ROWTILE: tiles of NT / VR rows; one wave of resident CTAs striding over
-// the tiles (each prefetches its next tile's row bounds). LX lists rows
-// longer than one window for the chunk kernel.
-template <typename VT, typename IT, int VR>
-static pf_status launch_rowtile(pf_handle h, const SpmvParams<VT, IT> &prm, bool lx,
-                                cudaStream_t st) {
-  constexpr int NT = kRowTileNT, CAP = kRowTileCap, MINB = PF_RT_MINB;
-  constexpr int R = NT / VR;
-  static int occ_dev[kMaxDevices][2] = {};
-  int &occ = occ_dev[h->device % kMaxDevices][lx ? 1 : 0];
-  if (occ == 0) {
-    int o = 0;
-    if (lx)
-      PF_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-          &o, spmv_rowtile_kernel<VT, IT, NT, VR, CAP, true, MINB>, NT, 0));
-    else
-      PF_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-          &o, spmv_rowtile_kernel<VT, IT, NT, VR, CAP, false, MINB>, NT, 0));
-    occ = std::max(1, o);
-  }
-  const int64_t tiles = ceil_div(prm.m, (int64_t)R);
-  const unsigned grid =
-      (unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)h->num_sms * occ));
-  if (!lx) {
-    spmv_rowtile_kernel<VT, IT, NT, VR, CAP, false, MINB>
-        <<<grid, NT, 0, st>>>(prm, LongRowScratch{}, INT64_MAX, kLxChunk);
-    count_launch();
-    PF_CUDA_TRY(cudaGetLastError());
-    return PF_OK;
-  }
-  const int64_t lt = CAP;
-  pf_status s = ensure_lx(h, prm.nnz, lt, kLxChunk, st);
-  if (s != PF_OK) return s;
-  spmv_rowtile_kernel<VT, IT, NT, VR, CAP, true, MINB><<<grid, NT, 0, st>>>(prm, h->lx, lt, kLxChunk);
   launch_chunks<VT, IT>(h, prm, st);
   count_launch(2);
   PF_CUDA_TRY(cudaGetLastError());
@@ -538,25 +475,6 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
       (((uintptr_t)col | (uintptr_t)val) & 15) != 0) {
     ch.variant = PF_VARIANT_ROWGROUP;
     ch.lanes = rowgroup_lanes(m > 0 ? (double)nnz / (double)m : 0.0);
-  }
-  // ROWTILE_LX's chunk kernel needs 16-byte aligned col/val (16-byte
-  // blocks); ROWTILE itself loads elements
-  if (ch.variant == PF_VARIANT_ROWTILE_LX && (((uintptr_t)col | (uintptr_t)val) & 15) != 0)
-    ch.variant = PF_VARIANT_ROWTILE;
-  if (ch.variant == PF_VARIANT_ROWTILE || ch.variant == PF_VARIANT_ROWTILE_LX) {
-    const bool lx = ch.variant == PF_VARIANT_ROWTILE_LX;
-    prm.T = 0;
-    prm.num_ctas = 0;
-    prm.carry_head = prm.carry_tail = nullptr;
-    prm.counters = nullptr;
-    switch (ch.lanes) {
-      case 1: return launch_rowtile<VT, IT, 1>(h, prm, lx, st);
-      case 2: return launch_rowtile<VT, IT, 2>(h, prm, lx, st);
-      case 4: return launch_rowtile<VT, IT, 4>(h, prm, lx, st);
-      case 8: return launch_rowtile<VT, IT, 8>(h, prm, lx, st);
-      case 16: return launch_rowtile<VT, IT, 16>(h, prm, lx, st);
-      default: return launch_rowtile<VT, IT, 32>(h, prm, lx, st);
-    }
   }
   if (ch.variant == PF_VARIANT_ROWVEC || ch.variant == PF_VARIANT_ROWVEC_LX) {
     const bool lx = ch.variant == PF_VARIANT_ROWVEC_LX;
@@ -884,7 +802,8 @@ pf_status pf_handle_destroy(pf_handle h) {
 
 pf_status pf_handle_set_variant(pf_handle h, int variant) {
   PF_CHECK_ARG(h != nullptr, "null handle");
-  PF_CHECK_ARG(variant >= PF_VARIANT_AUTO && variant <= PF_VARIANT_WARPSPLIT,
+  PF_CHECK_ARG(variant >= PF_VARIANT_AUTO && variant <= PF_VARIANT_WARPSPLIT && variant != 6 &&
+                   variant != 7,
                "unknown variant %d", variant);
   h->variant = variant;
   return PF_OK;

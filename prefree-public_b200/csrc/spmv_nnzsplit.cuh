@@ -50,7 +50,7 @@ struct SpmvParams {
   unsigned *err;        // device error word
 };
 
-// Long-row escape (ROWVEC_LX, ROWTILE_LX): rows longer than the short-row
+// Long-row escape (ROWVEC_LX): rows longer than the short-row
 // limit are cut into chunks of at most `chunk` non-zeros by the row kernel,
 // which writes one descriptor per chunk; the chunk kernel sums the chunks.
 // Chunk ids are reserved with a 64-bit atomic counter. All counters are zero

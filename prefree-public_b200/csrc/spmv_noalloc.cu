@@ -15,8 +15,10 @@
 // loads the library holds it (about 41 KB) until the process exits.
 //
 // Limits and rules:
-//   * at most kNoAllocMaxSlices CTA slices; the slice count is the SM count
-//     times the kernel's occupancy (444 on a B200), larger counts are refused;
+//   * at most kNoAllocMaxSlices CTA slices; the slice count is at most the SM
+//     count times the kernel's occupancy (444 on a B200), so the limit only
+//     binds on a GPU with far more SMs; larger counts are refused with
+//     PF_ERR_UNSUPPORTED;
 //   * the first call on a device does a one-time set-up with that device
 //     current (it looks up the array's device address with
 //     cudaGetSymbolAddress and sets the kernel's shared-memory limit); make
@@ -24,8 +26,10 @@
 //   * every call shares the one array: calls that overlap on the GPU (two
 //     host threads, two streams) race and give wrong results. Each call
 //     clears the counters and the error word it uses before its launch;
-//   * the call returns once the multiply has finished on `stream` (it waits
-//     for the stream so that it can report the kernel's error word).
+//   * every call (the nnz = 0 one too) returns once its work has finished on
+//     `stream`: it waits for the stream so that it can report the kernel's
+//     error word, PF_ERR_DEVICE when a bit is set (for example when
+//     row_ptr[m] - row_ptr[0] != nnz; nothing is written then).
 #include <mutex>
 
 #include "pf_common.cuh"
@@ -110,6 +114,7 @@ extern "C" pf_status pf_spmv_noalloc_f64_i32(int64_t m, int64_t n, int64_t nnz,
     scale_rows_kernel<double><<<blocks, 256, 0, st>>>(m, beta, y);
     count_launches(1);
     PF_CUDA_TRY(cudaGetLastError());
+    PF_CUDA_TRY(cudaStreamSynchronize(st));  // returns after the work, as every call does
     return PF_OK;
   }
 

@@ -72,7 +72,7 @@ def check(oracle, y, rp, col, val, x, vdt, alpha=1.0, beta=0.0, y0=None):
 
 
 VARIANTS = {"auto": 0, "nnzsplit": 1, "rowgroup": 2, "nnzsplit_ldg": 3, "rowvec": 4,
-            "rowvec_lx": 5, "rowtile": 6, "rowtile_lx": 7, "warpsplit": 8}
+            "rowvec_lx": 5, "warpsplit": 8}
 
 
 @pytest.fixture
@@ -107,7 +107,7 @@ def test_small_slices_force_cut_rows(pf, oracle, torch_cuda, variant_handle, nam
 
 
 @pytest.mark.parametrize("variant_handle", ["nnzsplit", "rowgroup", "rowvec", "rowvec_lx",
-                                            "rowtile", "rowtile_lx", "warpsplit"],
+                                            "warpsplit"],
                          indirect=True)
 @pytest.mark.parametrize("offset", [1, 2, 3, 5])
 def test_unaligned_array_starts(pf, oracle, torch_cuda, variant_handle, offset):
