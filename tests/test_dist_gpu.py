@@ -1,8 +1,8 @@
 """Row-sharded iterated multiply on GPUs: the fused multiply + all-gather
 (pf_spmv_dist_*: rows stored straight into every rank's next x, ||y||^2
 reduced in the kernel) against the unfused path (pf_spmv + NCCL all-gather)
-and against the CPU oracle's power iteration. The 2-GPU case spawns NCCL
-ranks and is skipped when fewer than two GPUs are visible."""
+and against the CPU oracle's power iteration. The multi-GPU cases spawn one
+NCCL rank per GPU and are skipped when fewer GPUs are visible."""
 import os
 import socket
 import sys
@@ -16,8 +16,10 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 STEPS = 5
 
 
-def small_spec(pf):
-    return pf.GenSpec(cfg=5, seed=77, m=1 << 15, n=1 << 15)
+def small_spec(pf, cfg=5):
+    """Config 5 (banded + uniform, equal shards) or config 3 (power-law rows:
+    equal-nnz shards of unequal row counts) at 2^15 rows."""
+    return pf.GenSpec(cfg=cfg, seed=77, m=1 << 15, n=1 << 15)
 
 
 def oracle_iterates(pf, oracle, spec, steps):
@@ -77,7 +79,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, q):
+def _rank_main(rank, world, port, q, cfg=5, index_bits=64):
     sys.path.insert(0, ROOT)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), NCCL_NVLS_ENABLE="0")
@@ -91,10 +93,11 @@ def _rank_main(rank, world, port, q):
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
         pf = importlib.import_module("prefree-public_b200")
         pfd = importlib.import_module("prefree-public_b200.dist")
-        spec = small_spec(pf).resolved()
+        spec = small_spec(pf, cfg).resolved()
         b = pfd.gen_bounds(pf, spec, world)
         r0, r1 = int(b[rank]), int(b[rank + 1])
-        rp, col, val = pf.gen_rows_device(spec, r0, r1, index_dtype=torch.int64, device=dev)
+        idt = torch.int64 if index_bits == 64 else torch.int32
+        rp, col, val = pf.gen_rows_device(spec, r0, r1, index_dtype=idt, device=dev)
         x0 = pf.gen_x_device(spec, device=dev)
         h = pf.Handle()
         fused = pfd.FusedPowerIteration(pf, h, rp, col, val, x0, b, rank, world)
@@ -119,28 +122,36 @@ def _rank_main(rank, world, port, q):
         q.put((rank, "error", repr(e), None, None, None, None))
 
 
-def test_two_gpus_fused_and_nccl_match_oracle(pf, oracle):
+@pytest.mark.parametrize("world,cfg,index_bits", [(2, 5, 64), (2, 3, 32), (4, 3, 32),
+                                                  (4, 5, 64)])
+def test_multi_gpu_fused_and_nccl_match_oracle(pf, oracle, world, cfg, index_bits):
+    """world ranks, one per GPU (spawned NCCL processes, NVLS off): the fused
+    step and the NCCL path both reproduce the CPU oracle's power iteration.
+    Config 3 gives equal-nnz shards of unequal row counts (the NCCL path then
+    all-gathers through broadcasts) and runs the int32 row_ptr kernels."""
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_rank_main, args=(r, world, port, q, cfg, index_bits))
+          for r in range(world)]
     [p.start() for p in ps]
-    res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
+    res = sorted([q.get(timeout=300) for _ in range(world)], key=lambda r: r[0])
     [p.join(timeout=60) for p in ps]
     for p in ps:
         if p.is_alive():
             p.kill()
     assert all(r[1] == "ok" for r in res), res
-    xr, nr = oracle_iterates(pf, oracle, small_spec(pf), STEPS)
+    xr, nr = oracle_iterates(pf, oracle, small_spec(pf, cfg), STEPS)
     for rank, _, xf, xu, nf, nu, err in res:
         assert err == 0
         assert close(xf, xr) and close(xu, xr), rank
         assert np.allclose(nf, nr, rtol=1e-12) and np.allclose(nu, nr, rtol=1e-12)
-    assert np.array_equal(res[0][2], res[1][2])       # every rank holds the same x
+    for r in res[1:]:
+        assert np.array_equal(res[0][2], r[2])       # every rank holds the same x
 
 
 def test_step_barrier_times_out_without_peer(pf):
