@@ -48,7 +48,8 @@ typedef enum pf_variant {
   PF_VARIANT_NNZSPLIT_LDG = 3, /* NNZSPLIT with plain coalesced loads (no TMA) */
   PF_VARIANT_ROWVEC = 4,   /* row-aligned, 16-byte block loads per lane        */
   PF_VARIANT_ROWVEC_LX = 5, /* ROWVEC + long rows finished in balanced chunks  */
-  /* 6 and 7 are unused (variants measured slower everywhere and removed) */
+  PF_VARIANT_NNZTILE = 6,  /* nnz slices in register tiles, CTA segmented scan */
+  /* 7 is unused */
   PF_VARIANT_WARPSPLIT = 8  /* nnz-balanced slices per warp, any row length     */
 } pf_variant;
 

@@ -9,6 +9,7 @@
 
 #include "pf_common.cuh"
 #include "spmv_nnzsplit.cuh"
+#include "spmv_nnztile.cuh"
 #include "spmv_rowgroup.cuh"
 #include "spmv_rowvec.cuh"
 #include "spmv_tma.cuh"
@@ -272,6 +273,8 @@ static pf_status select_variant(pf_handle h, int64_t m, int64_t nnz, const IT *r
 
 template <typename VT, typename IT>
 static pf_status launch_warpsplit(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st);
+template <typename VT, typename IT>
+static pf_status launch_nnztile(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st);
 
 // The long-row chunk kernel: a full wave of resident CTAs (warps stride
 // over the chunk list, so more CTAs only add waves of idle warps).
@@ -462,6 +465,11 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
   prm.beta = beta;
   prm.err = h->err;
 
+  // NNZTILE needs 16-byte aligned col/val (16-byte block loads)
+  if (ch.variant == PF_VARIANT_NNZTILE) {
+    if ((((uintptr_t)col | (uintptr_t)val) & 15) == 0) return launch_nnztile<VT, IT>(h, prm, st);
+    ch.variant = PF_VARIANT_NNZSPLIT_LDG;
+  }
   // WARPSPLIT needs 16-byte aligned col/val (16-byte block loads)
   if (ch.variant == PF_VARIANT_WARPSPLIT) {
     if ((((uintptr_t)col | (uintptr_t)val) & 15) == 0) return launch_warpsplit<VT, IT>(h, prm, st);
@@ -579,6 +587,49 @@ static pf_status launch_warpsplit(pf_handle h, SpmvParams<VT, IT> prm, cudaStrea
   prm.counters = h->counters;
   const int64_t grid = std::min<int64_t>(ceil_div(P, NTB / 32), (int64_t)h->num_sms * occ);
   kern<<<(unsigned)grid, NTB, smem, st>>>(prm);
+  count_launch();
+  PF_CUDA_TRY(cudaGetLastError());
+  return PF_OK;
+}
+
+// NNZTILE shape: threads per CTA, non-zeros per thread, CTAs per SM
+#ifndef PF_NT_NT
+#define PF_NT_NT 128
+#endif
+#ifndef PF_NT_E
+#define PF_NT_E 4
+#endif
+#ifndef PF_NT_MINB
+#define PF_NT_MINB 12
+#endif
+
+// NNZTILE: one wave of resident CTAs, one equal-nnz slice each (at least
+// one tile).
+template <typename VT, typename IT>
+static pf_status launch_nnztile(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st) {
+  constexpr int NT = PF_NT_NT, E = PF_NT_E, MINB = PF_NT_MINB;
+  auto kern = spmv_nnztile_kernel<VT, IT, NT, E, MINB>;
+  static int occ_dev[kMaxDevices] = {};
+  int &occ = occ_dev[h->device % kMaxDevices];
+  if (occ == 0) {
+    int o = 0;
+    PF_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, NT, 0));
+    occ = std::max(1, o);
+  }
+  const int64_t ctas = (int64_t)h->num_sms * occ;
+  const int64_t T = h->slice_override > 0 ? h->slice_override
+                                          : std::max<int64_t>(ceil_div(prm.nnz, ctas), (int64_t)NT * E);
+  const int64_t P = ceil_div(prm.nnz, T);
+  PF_CHECK_ARG(P <= INT32_MAX, "too many slices");
+  PF_CHECK_ARG(T < INT32_MAX, "slice too long");
+  pf_status s = ensure_scratch(h, P, st);
+  if (s != PF_OK) return s;
+  prm.T = T;
+  prm.num_ctas = P;
+  prm.carry_head = h->carry;
+  prm.carry_tail = h->carry + h->cap;
+  prm.counters = h->counters;
+  kern<<<(unsigned)P, NT, 0, st>>>(prm);
   count_launch();
   PF_CUDA_TRY(cudaGetLastError());
   return PF_OK;
@@ -802,8 +853,7 @@ pf_status pf_handle_destroy(pf_handle h) {
 
 pf_status pf_handle_set_variant(pf_handle h, int variant) {
   PF_CHECK_ARG(h != nullptr, "null handle");
-  PF_CHECK_ARG(variant >= PF_VARIANT_AUTO && variant <= PF_VARIANT_WARPSPLIT && variant != 6 &&
-                   variant != 7,
+  PF_CHECK_ARG(variant >= PF_VARIANT_AUTO && variant <= PF_VARIANT_WARPSPLIT && variant != 7,
                "unknown variant %d", variant);
   h->variant = variant;
   return PF_OK;
