@@ -599,16 +599,24 @@ def main():
             pf.spmv_host(he, a_rp, a_col, a_val, a_x, a_y, stream=stream.cuda_stream)
         e1.record(stream)
         torch.cuda.synchronize()
-        e_ms = torch.tensor([e0.elapsed_time(e1) / ks], dtype=torch.float64, device=dev)
+        my_ms = e0.elapsed_time(e1) / ks
+        my_h2d = h_rp.numel() * 8 + h_col.numel() * 4 + h_val.numel() * 8 + h_x.numel() * 8
+        e_ms = torch.tensor([my_ms], dtype=torch.float64, device=dev)
+        # per-rank host-to-device rate (the rank's shard and its own full x,
+        # which every row of the shard may read): min and max over ranks
+        rate = torch.tensor([my_h2d / (my_ms * 1e-3) / 1e9], dtype=torch.float64, device=dev)
+        rate_min, rate_max = rate.clone(), rate.clone()
         if world > 1:
             dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
-        h2d = torch.tensor([h_rp.numel() * 8 + h_col.numel() * 4 + h_val.numel() * 8 +
-                            h_x.numel() * 8, h_y.numel() * 8], dtype=torch.int64, device=dev)
+            dist.all_reduce(rate_min, op=dist.ReduceOp.MIN)
+            dist.all_reduce(rate_max, op=dist.ReduceOp.MAX)
+        h2d = torch.tensor([my_h2d, h_y.numel() * 8], dtype=torch.int64, device=dev)
         if world > 1:
             dist.all_reduce(h2d)
         e2e = {"value": 2.0 * z_tot / (float(e_ms) * 1e-3) / 1e9, "unit": "GFLOP/s",
                "h2d_bytes_per_step": int(h2d[0]), "d2h_bytes_per_step": int(h2d[1]),
                "ms_per_step": float(e_ms), "steps": ks,
+               "h2d_GBps_per_rank": {"min": float(rate_min), "max": float(rate_max)},
                "call": "pf_spmv_host_f64_i64 per rank on its host shard (one multiply)"}
         he.close()
         del h_rp, h_col, h_val, h_x, h_y
