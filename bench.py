@@ -538,6 +538,8 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    if args.path == "fused":
+        h.dist_wait_ns(reset=True)
     launches0 = pf.launch_count()
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
@@ -551,6 +553,20 @@ def main():
         dist.barrier()
     launches = pf.launch_count() - launches0
     step_ms = t_start.elapsed_time(t_end) / args.steps
+    dist_diag = None
+    if args.path == "fused" and world > 1:
+        # how long each rank's CTAs waited in the in-kernel step barrier, and
+        # each rank's own kernel time: min / max over ranks
+        wns, ctas = h.dist_wait_ns(reset=True)
+        my_kern = sum(a.elapsed_time(b) for a, b in ev_pairs) / len(ev_pairs)
+        d = torch.tensor([wns / max(ctas, 1) / args.steps / 1e3, my_kern], dtype=torch.float64,
+                         device=dev)
+        dmin, dmax = d.clone(), d.clone()
+        dist.all_reduce(dmin, op=dist.ReduceOp.MIN)
+        dist.all_reduce(dmax, op=dist.ReduceOp.MAX)
+        dist_diag = {"barrier_wait_us_per_cta_step": {"min": float(dmin[0]), "max": float(dmax[0])},
+                     "kernel_ms_per_rank": {"min": float(dmin[1]), "max": float(dmax[1])},
+                     "ctas_per_rank": ctas}
     if args.path == "fused":
         final_nsq = fused.norm_sq()
     else:
@@ -665,6 +681,7 @@ def main():
             "clocks": clocks.summary(),
             "check": {"final_norm_sq_of_y": final_nsq, "final_norm": final_norm},
             "per_config": per,
+            "dist": dist_diag,
         }
         print(json.dumps(out), flush=True)
     h.close()

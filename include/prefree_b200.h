@@ -189,6 +189,11 @@ pf_status pf_spmv_dist_f64_i32(pf_handle h, int64_t m, int64_t n, int64_t nnz,
                                int nranks, int rank, double *const *out_ptrs,
                                double *const *slot_ptrs, int64_t row_offset,
                                uint64_t *const *flag_ptrs, uint64_t step, void *stream);
+/* Nanoseconds the fused steps of this handle spent in their in-kernel step
+ * barrier, summed over CTAs and steps since the last reset, and the CTAs of
+ * the last fused launch (a diagnostic of how long ranks wait for one
+ * another). Synchronizes the device. */
+pf_status pf_handle_dist_wait(pf_handle h, uint64_t *wait_ns, int64_t *ctas, int reset);
 
 /* ---- allocation-free multiply (fp64 values, int32 row_ptr) ------------------
  * No counterpart in the reference. For callers that cannot allocate device

@@ -36,7 +36,7 @@ EXPORTED = [
     "pf_last_error", "pf_version", "pf_launch_count",
     "pf_handle_create", "pf_handle_destroy", "pf_handle_set_variant",
     "pf_handle_set_slice", "pf_handle_device_error", "pf_handle_choice_i32",
-    "pf_handle_choice_i64",
+    "pf_handle_choice_i64", "pf_handle_dist_wait",
     "pf_spmv_f64_i32", "pf_spmv_f64_i64", "pf_spmv_f32_i32", "pf_spmv_f32_i64",
     "pf_spmv_host_f64_i32", "pf_spmv_host_f64_i64", "pf_spmv_host_f32_i32",
     "pf_spmv_host_f32_i64",
@@ -84,6 +84,8 @@ def _load():
     lib.pf_handle_set_variant.argtypes = [vp, C.c_int]
     lib.pf_handle_set_slice.argtypes = [vp, i64]
     lib.pf_handle_device_error.argtypes = [vp, C.POINTER(C.c_uint32), C.c_int]
+    lib.pf_handle_dist_wait.argtypes = [vp, C.POINTER(C.c_uint64), C.POINTER(i64), C.c_int]
+    lib.pf_handle_dist_wait.restype = st
     for name in ("pf_handle_choice_i32", "pf_handle_choice_i64"):
         getattr(lib, name).argtypes = [vp, i64, i64, vp, vp, C.POINTER(C.c_int),
                                        C.POINTER(C.c_int)]
@@ -201,6 +203,14 @@ class Handle:
         _check(fn(self._h, int(m), int(nnz), row_ptr.data_ptr(), C.c_void_p(stream),
                   C.byref(v), C.byref(ln)))
         return VARIANT_NAMES[v.value], int(ln.value)
+
+    def dist_wait_ns(self, reset: bool = True) -> tuple[int, int]:
+        """(nanoseconds the fused steps spent in their in-kernel step barrier,
+        summed over CTAs and steps; CTAs of the last fused launch).
+        Synchronizes the device."""
+        v, g = C.c_uint64(), C.c_int64()
+        _check(lib.pf_handle_dist_wait(self._h, C.byref(v), C.byref(g), int(reset)))
+        return int(v.value), int(g.value)
 
     def close(self):
         if self._h:

@@ -81,6 +81,8 @@ struct pf_handle_s {
   // fused all-gather: per-CTA norm partials + counter (zeroed when grown)
   double *dist_part = nullptr;
   unsigned *dist_counter = nullptr;
+  unsigned long long *dist_wait = nullptr;  // step-barrier wait, ns summed over CTAs
+  int64_t dist_grid = 0;                    // CTAs of the last fused launch
   int64_t dist_cap = 0;
   pf::LongRowScratch lx{};
   // host-call buffers
@@ -349,12 +351,15 @@ static pf_status launch_rowvec_dist(pf_handle h, const SpmvParams<double, IT> &p
     h->dist_cap = 0;
     PF_CUDA_TRY(cudaMalloc(&h->dist_part, sizeof(double) * (size_t)grid + 256));
     h->dist_counter = (unsigned *)(h->dist_part + grid);
-    PF_CUDA_TRY(cudaMemsetAsync(h->dist_counter, 0, sizeof(unsigned), st));
+    h->dist_wait = (unsigned long long *)(h->dist_part + grid + 1);
+    PF_CUDA_TRY(cudaMemsetAsync(h->dist_counter, 0, 16, st));
     h->dist_cap = grid;
   }
   DistOut d = D;
   d.cta_part = h->dist_part;
   d.counter = h->dist_counter;
+  d.wait_ns = h->dist_wait;
+  h->dist_grid = grid;
   spmv_rowvec_kernel<double, IT, V, U, NTB, false, MINB, true>
       <<<(unsigned)grid, NTB, 0, st>>>(prm, LongRowScratch{}, INT64_MAX, kLxChunk, d);
   count_launch();
@@ -877,6 +882,19 @@ pf_status pf_handle_device_error(pf_handle h, uint32_t *bits, int clear) {
     h->scratch_dirty = true;  // a failed launch may leave counters set
     h->lx_dirty = true;
   }
+  return PF_OK;
+}
+
+pf_status pf_handle_dist_wait(pf_handle h, uint64_t *wait_ns, int64_t *ctas, int reset) {
+  PF_CHECK_ARG(h != nullptr && wait_ns != nullptr && ctas != nullptr, "null argument");
+  *wait_ns = 0;
+  *ctas = h->dist_grid;
+  if (!h->dist_wait) return PF_OK;
+  PF_CUDA_TRY(cudaDeviceSynchronize());
+  unsigned long long v = 0;
+  PF_CUDA_TRY(cudaMemcpy(&v, h->dist_wait, sizeof(v), cudaMemcpyDeviceToHost));
+  *wait_ns = v;
+  if (reset) PF_CUDA_TRY(cudaMemset(h->dist_wait, 0, sizeof(v)));
   return PF_OK;
 }
 

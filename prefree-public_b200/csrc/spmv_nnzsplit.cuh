@@ -122,6 +122,9 @@ struct DistOut {
   unsigned long long step;
   int64_t row_offset;
   int nranks, rank;
+  // nanoseconds the CTAs spent in the step barrier's wait, summed over CTAs
+  // and steps (a diagnostic; null: not counted)
+  unsigned long long *wait_ns;
 };
 
 // Bound of the step barrier's wait: far above any step (milliseconds); a

@@ -103,40 +103,51 @@ spmv_nnztile_kernel(const SpmvParams<VT, IT> P) {
     P.y[R] = (VT)out;
   };
 
+  // Positions inside the slice are 32-bit offsets from A, S0 rounded down to
+  // a 16-byte block (a slice holds fewer than 2^31 non-zeros); the tile's
+  // column and value blocks are addressed from there.
   const int64_t A = S0 & ~(int64_t)3;
-  const int ntiles = (int)((S1 - A + TILE - 1) / TILE);
+  const int lo0 = (int)(S0 - A), hiS = (int)(S1 - A);
+  const int4 *__restrict__ colA = reinterpret_cast<const int4 *>(P.col + A);
+  const VT *__restrict__ valA = P.val + A;
+  // a row_ptr entry as an offset from A, clamped to [-1, hiS + 1] (a row that
+  // ends past the slice compares as past it)
+  auto rel = [&](int64_t r) -> int {
+    const int64_t v = (int64_t)__ldg(P.row_ptr + r) - A;
+    return (int)min(max(v, (int64_t)-1), (int64_t)hiS + 1);
+  };
+  const int ntiles = (hiS + TILE - 1) / TILE;
   double carry = 0.0;  // sum of the open row so far (the same in every thread)
   for (int i = 0; i < ntiles; ++i) {
     const int par = i & 1;
-    const int64_t tb = A + (int64_t)i * TILE;
-    const int64_t lo = max(tb, S0), hi = min(tb + TILE, S1);
+    const int tb = i * TILE;
+    const int lo = max(tb, lo0), hi = min(tb + TILE, hiS);
     // ---- 1. this thread's column blocks and value pieces, the row window
-    const int64_t q0 = tb + (int64_t)E * tid;
+    const int q0 = tb + E * tid;
     int cc[E];
     VT vv[E];
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
-      const int64_t q = q0 + 4 * b;
+      const int q = q0 + 4 * b;
       const bool act = q + 4 > lo && q < hi;
-      const int4 c4 = act ? __ldcs(reinterpret_cast<const int4 *>(P.col + q)) : make_int4(0, 0, 0, 0);
+      const int4 c4 = act ? __ldcs(colA + (q >> 2)) : make_int4(0, 0, 0, 0);
       cc[4 * b] = c4.x;
       cc[4 * b + 1] = c4.y;
       cc[4 * b + 2] = c4.z;
       cc[4 * b + 3] = c4.w;
-      Block4<VT>::load(P.val, q, act && q + 2 > lo, act && q + 2 < hi, vv + 4 * b);
+      Block4<VT>::load(valA, q, act && q + 2 > lo, act && q + 2 < hi, vv + 4 * b);
     }
-    int64_t rs = 0, re = 0;
     bool have = r_cur + tid < P.m;
+    int rs = 0, re = 0;
     if (have) {
-      rs = (int64_t)__ldg(P.row_ptr + r_cur + tid);
-      re = (int64_t)__ldg(P.row_ptr + r_cur + tid + 1);
+      rs = rel(r_cur + tid);
+      re = rel(r_cur + tid + 1);
     }
     // ---- 2. x gathers and products
     double p[E];
 #pragma unroll
     for (int k = 0; k < E; ++k) {
-      const int64_t g = q0 + k;
-      const bool use = g >= lo && g < hi;
+      const bool use = q0 + k >= lo && q0 + k < hi;
       const bool inb = (uint32_t)cc[k] < n;
       bad |= use && !inb;
       const VT xv = (use && inb) ? ptx::ldg_x(P.x + cc[k]) : VT(0);
@@ -147,21 +158,16 @@ spmv_nnztile_kernel(const SpmvParams<VT, IT> P) {
     while (true) {
       // row r_cur + done + tid ends in this tile; an empty row that starts at
       // S1 belongs to the next slice (the last slice takes every row)
-      const bool fin = have && re <= hi && !(!last && re == rs && rs == S1);
+      const bool fin = have && re <= hi && !(!last && re == rs && rs == hiS);
       if (fin) {
-        const int64_t R = r_cur + done + tid;
-        if (re > rs) {
-          const int64_t pos = re - 1 - tb;
-          if (pos >= lo - tb && pos < hi - tb) {
-            atomicOr(&s_mask[par][pos >> 5], 1u << (pos & 31));
-            s_row[par][pos] = done + tid;
-          } else {
-            bad_rows = true;  // row_ptr not non-decreasing
-          }
+        if (re > rs && re > lo) {
+          const int pos = re - 1 - tb;
+          atomicOr(&s_mask[par][pos >> 5], 1u << (pos & 31));
+          s_row[par][pos] = done + tid;
         } else if (re == rs) {
-          write_row(R, 0.0);  // empty row (never the slice's head row)
+          write_row(r_cur + done + tid, 0.0);  // empty row (never the slice's head row)
         } else {
-          bad_rows = true;
+          bad_rows = true;  // row_ptr not non-decreasing
         }
       }
       const int nf = __syncthreads_count(fin);
@@ -170,30 +176,26 @@ spmv_nnztile_kernel(const SpmvParams<VT, IT> P) {
       // every row of the window ends here: the next window
       have = r_cur + done + tid < P.m;
       if (have) {
-        rs = (int64_t)__ldg(P.row_ptr + r_cur + done + tid);
-        re = (int64_t)__ldg(P.row_ptr + r_cur + done + tid + 1);
+        rs = rel(r_cur + done + tid);
+        re = rel(r_cur + done + tid + 1);
       }
     }
-    // ---- 4. walk the products against the mask bits
+    // ---- 4. walk the products against the mask bits: a row that ends and
+    // is not the thread's first is written at once
     constexpr uint32_t LMASK = (1u << E) - 1u;
     const uint32_t bits = (s_mask[par][(E * tid) >> 5] >> ((E * tid) & 31)) & LMASK;
     double acc = 0.0, head = 0.0;
-    int first = -1;
+    const int first = bits ? __ffs(bits) - 1 : E;
 #pragma unroll
     for (int k = 0; k < E; ++k) {
       acc += p[k];
-      if ((bits >> k) & 1u) {
-        if (first < 0) {
-          head = acc;
-          first = k;
-        } else {
-          write_row(r_cur + s_row[par][E * tid + k], acc);
-        }
-        acc = 0.0;
-      }
+      const bool end = (bits >> k) & 1u;
+      if (end && k > first) write_row(r_cur + s_row[par][E * tid + k], acc);
+      head = (k == first) ? acc : head;
+      acc = end ? 0.0 : acc;
     }
     // segmented scan over the CTA: (ended a row, sum since its last end)
-    int f = first >= 0 ? 1 : 0;
+    int f = bits ? 1 : 0;
     double v = acc;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
@@ -222,7 +224,7 @@ spmv_nnztile_kernel(const SpmvParams<VT, IT> P) {
     const double incl = f ? v : pf_v + v;
     double excl = __shfl_up_sync(0xffffffffu, incl, 1);
     if (lane == 0) excl = pf_v;
-    if (first >= 0) {
+    if (bits) {
       const int64_t R = r_cur + s_row[par][E * tid + first];
       if (R == head_row) contribute_cut_row(P, base, R, true, c, excl + head);
       else write_row(R, excl + head);
@@ -234,7 +236,7 @@ spmv_nnztile_kernel(const SpmvParams<VT, IT> P) {
     if (tid < MW) s_mask[par][tid] = 0u;
   }
   // the row still open at the slice end runs past S1: hand on its partial
-  if (tid == 0 && !last && r_cur < P.m && (int64_t)__ldg(P.row_ptr + r_cur) < S1)
+  if (tid == 0 && !last && r_cur < P.m && rel(r_cur) < hiS)
     contribute_cut_row(P, base, r_cur, r_cur == head_row, c, carry);
   if (bad) atomicOr(P.err, PF_DEVERR_BOUNDS);
   if (bad_rows) atomicOr(P.err, PF_DEVERR_ROWPTR);

@@ -222,6 +222,7 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
           }
         }
         __threadfence_system();  // the peers' stores before this CTA's reads
+        if (D.wait_ns) atomicAdd(D.wait_ns, (unsigned long long)(ptx::globaltimer_ns() - t0));
       }
       __syncthreads();
     }
