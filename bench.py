@@ -285,7 +285,7 @@ def per_config_block(pf, torch, dev, with_cpu: bool):
         cold = time_cold_us(torch, ours, flush) if cfg in (1, 3) else None
         assert h.device_error() == 0, "device error word set"
         B = compulsory_bytes(spec.m, spec.n, z, val.element_size(), 4)
-        e = {"m": spec.m, "nnz": z, "variant": "%s/%d" % h.choice(spec.m, z, rp),
+        e = {"m": spec.m, "nnz": z, "variant": "%s/%d" % h.choice(spec.m, z, rp, val.element_size()),
              "alg_bytes": B, "us": warm, "gflops": 2 * z / warm / 1e3,
              "alg_GBps": B / warm / 1e3, "frac_of_" + peak_src: B / warm / 1e3 / hbm_peak,
              "frac_of_8TBps": B / warm / 1e3 / 8000.0}

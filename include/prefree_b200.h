@@ -73,15 +73,16 @@ pf_status pf_handle_set_slice(pf_handle h, int64_t slice_nnz);
 /* Synchronizes the device, returns the device error bits, optionally clears. */
 pf_status pf_handle_device_error(pf_handle h, uint32_t *bits, int clear);
 /* The variant (a pf_variant other than AUTO) and lanes per row that a
- * multiply with this handle would run for the device CSR (m, nnz, row_ptr):
- * the forced variant, or the selector's choice, which it computes (a sample
- * kernel on `stream`, synchronous) and caches as a multiply would. The
- * variant actually launched can still differ for arrays that are not 16-byte
- * aligned (each variant's fallback). */
+ * multiply with this handle would run for the device CSR (m, nnz, row_ptr)
+ * with values of value_bytes (2, 4 or 8) bytes: the forced variant, or the
+ * selector's choice, which it computes (a sample kernel on `stream`,
+ * synchronous) and caches as a multiply would. The variant actually
+ * launched can still differ for arrays that are not 16-byte aligned (each
+ * variant's fallback). */
 pf_status pf_handle_choice_i32(pf_handle h, int64_t m, int64_t nnz, const int32_t *row_ptr,
-                               void *stream, int *variant, int *lanes);
+                               int value_bytes, void *stream, int *variant, int *lanes);
 pf_status pf_handle_choice_i64(pf_handle h, int64_t m, int64_t nnz, const int64_t *row_ptr,
-                               void *stream, int *variant, int *lanes);
+                               int value_bytes, void *stream, int *variant, int *lanes);
 
 /* ---- device-pointer core: y = alpha*A*x + beta*y ----------------------------
  * row_ptr has m+1 entries; row_ptr[0] may be non-zero (a row slice of a larger

@@ -87,7 +87,7 @@ def _load():
     lib.pf_handle_dist_wait.argtypes = [vp, C.POINTER(C.c_uint64), C.POINTER(i64), C.c_int]
     lib.pf_handle_dist_wait.restype = st
     for name in ("pf_handle_choice_i32", "pf_handle_choice_i64"):
-        getattr(lib, name).argtypes = [vp, i64, i64, vp, vp, C.POINTER(C.c_int),
+        getattr(lib, name).argtypes = [vp, i64, i64, vp, C.c_int, vp, C.POINTER(C.c_int),
                                        C.POINTER(C.c_int)]
         getattr(lib, name).restype = st
     for name in ("pf_spmv_f64_i32", "pf_spmv_f64_i64", "pf_spmv_f32_i32", "pf_spmv_f32_i64",
@@ -189,10 +189,10 @@ class Handle:
         _check(lib.pf_handle_device_error(self._h, C.byref(bits), int(clear)))
         return int(bits.value)
 
-    def choice(self, m: int, nnz: int, row_ptr, stream=None):
+    def choice(self, m: int, nnz: int, row_ptr, value_bytes: int = 8, stream=None):
         """(variant name, lanes per row) this handle runs for the device
-        CSR with this row_ptr (a torch tensor): the forced variant or the
-        selector's cached choice."""
+        CSR with this row_ptr (a torch tensor) and values of value_bytes
+        bytes: the forced variant or the selector's cached choice."""
         import torch
         if stream is None:
             stream = torch.cuda.current_stream().cuda_stream
@@ -200,8 +200,8 @@ class Handle:
             stream = stream.cuda_stream
         v, ln = C.c_int(), C.c_int()
         fn = lib.pf_handle_choice_i64 if row_ptr.element_size() == 8 else lib.pf_handle_choice_i32
-        _check(fn(self._h, int(m), int(nnz), row_ptr.data_ptr(), C.c_void_p(stream),
-                  C.byref(v), C.byref(ln)))
+        _check(fn(self._h, int(m), int(nnz), row_ptr.data_ptr(), int(value_bytes),
+                  C.c_void_p(stream), C.byref(v), C.byref(ln)))
         return VARIANT_NAMES[v.value], int(ln.value)
 
     def dist_wait_ns(self, reset: bool = True) -> tuple[int, int]:

@@ -199,11 +199,13 @@ static int rowgroup_lanes(double avg) {
   return v;
 }
 
-// ROWVEC lanes: one 4-element block per lane covers an average row; long
-// rows use 16 lanes (measured faster than 32 on 2000-non-zero rows: more
-// rows in flight per warp)
+// ROWVEC lanes: two lanes take rows of up to 16 non-zeros (two 4-element
+// blocks each: measured faster than four lanes on 16-non-zero rows); longer
+// rows get one block per lane up to 16 lanes (measured faster than 32 on
+// 2000-non-zero rows: more rows in flight per warp)
 static int rowvec_lanes(double avg) {
-  int v = 2;
+  if (avg <= 16.0) return 2;
+  int v = 4;
   while (v < 16 && 4 * v < avg) v *= 2;
   return v;
 }
@@ -235,6 +237,16 @@ static pf_variant_choice choose_from_stats(int64_t m, int64_t nnz, const int64_t
     ch.variant = PF_VARIANT_WARPSPLIT;
     ch.lanes = 0;
   }
+  return ch;
+}
+
+// The selector's choice refined by the value size: for irregular rows,
+// WARPSPLIT with 8-byte values, NNZTILE with 4-byte ones (measured on the
+// power-law config: 183 against 196 us with fp32 values, a tie with fp64).
+// A forced variant is kept as it is.
+static pf_variant_choice for_values(pf_handle h, pf_variant_choice ch, int value_bytes) {
+  if (h->variant == PF_VARIANT_AUTO && ch.variant == PF_VARIANT_WARPSPLIT && value_bytes == 4)
+    ch.variant = PF_VARIANT_NNZTILE;
   return ch;
 }
 
@@ -451,6 +463,7 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
   pf_status s = select_variant<IT>(h, m, nnz, row_ptr, st, &ch);
   if (s != PF_OK) return s;
   constexpr bool kHalf = sizeof(VT) == 2;
+  ch = for_values(h, ch, (int)sizeof(VT));
   if (kHalf) {
     // 16-bit values run on the row-vector, warp-slice and plain-load kernels
     const double avg = (double)nnz / (double)m;
@@ -597,22 +610,13 @@ static pf_status launch_warpsplit(pf_handle h, SpmvParams<VT, IT> prm, cudaStrea
   return PF_OK;
 }
 
-// NNZTILE shape: threads per CTA, non-zeros per thread, CTAs per SM
-#ifndef PF_NT_NT
-#define PF_NT_NT 128
-#endif
-#ifndef PF_NT_E
-#define PF_NT_E 4
-#endif
-#ifndef PF_NT_MINB
-#define PF_NT_MINB 12
-#endif
-
 // NNZTILE: one wave of resident CTAs, one equal-nnz slice each (at least
 // one tile).
 template <typename VT, typename IT>
 static pf_status launch_nnztile(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st) {
-  constexpr int NT = PF_NT_NT, E = PF_NT_E, MINB = PF_NT_MINB;
+  // 128 threads, 8 non-zeros per thread, 10 CTAs per SM (48 registers): the
+  // best of a sweep over 64-256 threads, 4 or 8 non-zeros and 4-24 CTAs
+  constexpr int NT = 128, E = 8, MINB = 10;
   auto kern = spmv_nnztile_kernel<VT, IT, NT, E, MINB>;
   static int occ_dev[kMaxDevices] = {};
   int &occ = occ_dev[h->device % kMaxDevices];
@@ -899,22 +903,26 @@ pf_status pf_handle_dist_wait(pf_handle h, uint64_t *wait_ns, int64_t *ctas, int
 }
 
 pf_status pf_handle_choice_i32(pf_handle h, int64_t m, int64_t nnz, const int32_t *row_ptr,
-                               void *stream, int *variant, int *lanes) {
+                               int value_bytes, void *stream, int *variant, int *lanes) {
   PF_CHECK_ARG(h && variant && lanes && row_ptr && m > 0 && nnz > 0, "bad argument");
+  PF_CHECK_ARG(value_bytes == 2 || value_bytes == 4 || value_bytes == 8, "bad value size");
   pf_variant_choice ch;
   pf_status s = select_variant<int32_t>(h, m, nnz, row_ptr, (cudaStream_t)stream, &ch);
   if (s != PF_OK) return s;
+  ch = for_values(h, ch, value_bytes);
   *variant = ch.variant;
   *lanes = ch.lanes;
   return PF_OK;
 }
 
 pf_status pf_handle_choice_i64(pf_handle h, int64_t m, int64_t nnz, const int64_t *row_ptr,
-                               void *stream, int *variant, int *lanes) {
+                               int value_bytes, void *stream, int *variant, int *lanes) {
   PF_CHECK_ARG(h && variant && lanes && row_ptr && m > 0 && nnz > 0, "bad argument");
+  PF_CHECK_ARG(value_bytes == 2 || value_bytes == 4 || value_bytes == 8, "bad value size");
   pf_variant_choice ch;
   pf_status s = select_variant<int64_t>(h, m, nnz, row_ptr, (cudaStream_t)stream, &ch);
   if (s != PF_OK) return s;
+  ch = for_values(h, ch, value_bytes);
   *variant = ch.variant;
   *lanes = ch.lanes;
   return PF_OK;

@@ -91,8 +91,8 @@ def test_invalid_arguments_return_status_not_crash(pf):
                                None) == 1
     assert lib.pf_handle_set_variant(null, 0) == 1
     v, ln = C.c_int(), C.c_int()
-    assert lib.pf_handle_choice_i32(null, 4, 4, None, None, C.byref(v), C.byref(ln)) == 1
-    assert lib.pf_handle_choice_i64(null, 4, 4, None, None, C.byref(v), C.byref(ln)) == 1
+    assert lib.pf_handle_choice_i32(null, 4, 4, None, 8, None, C.byref(v), C.byref(ln)) == 1
+    assert lib.pf_handle_choice_i64(null, 4, 4, None, 8, None, C.byref(v), C.byref(ln)) == 1
     assert lib.pf_spmv_dist_f64_i64(null, 4, 4, 4, None, None, None, None, None, 1, 0, None,
                                     None, 0, None, 0, None) == 1
     t, p = C.c_double(), C.c_double()
