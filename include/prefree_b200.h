@@ -48,8 +48,8 @@ typedef enum pf_variant {
   PF_VARIANT_NNZSPLIT_LDG = 3, /* NNZSPLIT with plain coalesced loads (no TMA) */
   PF_VARIANT_ROWVEC = 4,   /* row-aligned, 16-byte block loads per lane        */
   PF_VARIANT_ROWVEC_LX = 5, /* ROWVEC + long rows finished in balanced chunks  */
-  PF_VARIANT_NNZTILE = 6,  /* nnz slices in register tiles, CTA segmented scan */
-  /* 7 is unused */
+  /* 6 is unused (measured slower everywhere and removed) */
+  PF_VARIANT_NNZROW = 7,   /* nnz slices, products in shared memory, row pieces summed */
   PF_VARIANT_WARPSPLIT = 8  /* nnz-balanced slices per warp, any row length     */
 } pf_variant;
 

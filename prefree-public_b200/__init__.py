@@ -26,10 +26,10 @@ PF_OK = 0
 STATUS_NAMES = {0: "PF_OK", 1: "PF_ERR_INVALID", 2: "PF_ERR_CUDA", 3: "PF_ERR_DEVICE",
                 4: "PF_ERR_UNSUPPORTED", 5: "PF_ERR_IO", 6: "PF_ERR_FORMAT"}
 (VARIANT_AUTO, VARIANT_NNZSPLIT, VARIANT_ROWGROUP, VARIANT_NNZSPLIT_LDG, VARIANT_ROWVEC,
- VARIANT_ROWVEC_LX, VARIANT_NNZTILE) = range(7)
-VARIANT_WARPSPLIT = 8  # 7 is unused
+ VARIANT_ROWVEC_LX) = range(6)
+VARIANT_NNZROW, VARIANT_WARPSPLIT = 7, 8  # 6 is unused
 VARIANT_NAMES = ["auto", "nnzsplit", "rowgroup", "nnzsplit_ldg", "rowvec", "rowvec_lx",
-                 "nnztile", "unused7", "warpsplit"]
+                 "unused6", "nnzrow", "warpsplit"]
 
 # every extern "C" symbol include/*.h declares (checked by the CPU tests)
 EXPORTED = [

@@ -9,7 +9,7 @@
 
 #include "pf_common.cuh"
 #include "spmv_nnzsplit.cuh"
-#include "spmv_nnztile.cuh"
+#include "spmv_nnzrow.cuh"
 #include "spmv_rowgroup.cuh"
 #include "spmv_rowvec.cuh"
 #include "spmv_tma.cuh"
@@ -227,26 +227,25 @@ static pf_variant_choice choose_from_stats(int64_t m, int64_t nnz, const int64_t
   for (int i = 0; i < S; ++i) mx = std::max(mx, sample[i]);
   pf_variant_choice ch;
   // regular rows (the sample never strays far above the mean): whole rows per
-  // lane group. Otherwise equal-nnz slices per warp: on the power-law config
-  // 2x faster than ROWVEC_LX, whose row kernel waits on each step's longest
-  // short row.
+  // lane group. Otherwise equal-nnz slices per CTA (NNZROW): on the power-law
+  // config 196 us against 216 for the per-warp slices of WARPSPLIT and ~430
+  // for ROWVEC_LX, whose row kernel waits on each step's longest short row.
   if (mx <= 4.0 * avg + 32.0) {
     ch.variant = PF_VARIANT_ROWVEC;
     ch.lanes = rowvec_lanes(avg);
   } else {
-    ch.variant = PF_VARIANT_WARPSPLIT;
+    ch.variant = PF_VARIANT_NNZROW;
     ch.lanes = 0;
   }
   return ch;
 }
 
-// The selector's choice refined by the value size: for irregular rows,
-// WARPSPLIT with 8-byte values, NNZTILE with 4-byte ones (measured on the
-// power-law config: 183 against 196 us with fp32 values, a tie with fp64).
-// A forced variant is kept as it is.
+// The selector's choice refined by the value size (every value size takes
+// the same kernels today; kept as the one place for such a rule). A forced
+// variant is kept as it is.
 static pf_variant_choice for_values(pf_handle h, pf_variant_choice ch, int value_bytes) {
-  if (h->variant == PF_VARIANT_AUTO && ch.variant == PF_VARIANT_WARPSPLIT && value_bytes == 4)
-    ch.variant = PF_VARIANT_NNZTILE;
+  (void)h;
+  (void)value_bytes;
   return ch;
 }
 
@@ -288,7 +287,7 @@ static pf_status select_variant(pf_handle h, int64_t m, int64_t nnz, const IT *r
 template <typename VT, typename IT>
 static pf_status launch_warpsplit(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st);
 template <typename VT, typename IT>
-static pf_status launch_nnztile(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st);
+static pf_status launch_nnzrow(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st);
 
 // The long-row chunk kernel: a full wave of resident CTAs (warps stride
 // over the chunk list, so more CTAs only add waves of idle warps).
@@ -483,11 +482,7 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
   prm.beta = beta;
   prm.err = h->err;
 
-  // NNZTILE needs 16-byte aligned col/val (16-byte block loads)
-  if (ch.variant == PF_VARIANT_NNZTILE) {
-    if ((((uintptr_t)col | (uintptr_t)val) & 15) == 0) return launch_nnztile<VT, IT>(h, prm, st);
-    ch.variant = PF_VARIANT_NNZSPLIT_LDG;
-  }
+  if (ch.variant == PF_VARIANT_NNZROW) return launch_nnzrow<VT, IT>(h, prm, st);
   // WARPSPLIT needs 16-byte aligned col/val (16-byte block loads)
   if (ch.variant == PF_VARIANT_WARPSPLIT) {
     if ((((uintptr_t)col | (uintptr_t)val) & 15) == 0) return launch_warpsplit<VT, IT>(h, prm, st);
@@ -610,14 +605,16 @@ static pf_status launch_warpsplit(pf_handle h, SpmvParams<VT, IT> prm, cudaStrea
   return PF_OK;
 }
 
-// NNZTILE: one wave of resident CTAs, one equal-nnz slice each (at least
-// one tile).
+// NNZROW: one wave of resident CTAs, one equal-nnz slice each (at least one
+// tile).
 template <typename VT, typename IT>
-static pf_status launch_nnztile(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st) {
-  // 128 threads, 8 non-zeros per thread, 10 CTAs per SM (48 registers): the
-  // best of a sweep over 64-256 threads, 4 or 8 non-zeros and 4-24 CTAs
-  constexpr int NT = 128, E = 8, MINB = 10;
-  auto kern = spmv_nnztile_kernel<VT, IT, NT, E, MINB>;
+static pf_status launch_nnzrow(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st) {
+  // 64 threads, 8 non-zeros per thread, pieces of more than 64 products to
+  // a warp, 16 CTAs per SM: the best of a sweep over 64-256 threads, 4 or 8
+  // non-zeros per thread, 16-64 products per thread piece, 4-32 CTAs per SM
+  // and 1-4 accumulators per piece
+  constexpr int NT = 64, K = 8, LS = 64, MINB = 16;
+  auto kern = spmv_nnzrow_kernel<VT, IT, NT, K, LS, MINB>;
   static int occ_dev[kMaxDevices] = {};
   int &occ = occ_dev[h->device % kMaxDevices];
   if (occ == 0) {
@@ -627,7 +624,7 @@ static pf_status launch_nnztile(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_
   }
   const int64_t ctas = (int64_t)h->num_sms * occ;
   const int64_t T = h->slice_override > 0 ? h->slice_override
-                                          : std::max<int64_t>(ceil_div(prm.nnz, ctas), (int64_t)NT * E);
+                                          : std::max<int64_t>(ceil_div(prm.nnz, ctas), (int64_t)NT * K);
   const int64_t P = ceil_div(prm.nnz, T);
   PF_CHECK_ARG(P <= INT32_MAX, "too many slices");
   PF_CHECK_ARG(T < INT32_MAX, "slice too long");
@@ -862,7 +859,7 @@ pf_status pf_handle_destroy(pf_handle h) {
 
 pf_status pf_handle_set_variant(pf_handle h, int variant) {
   PF_CHECK_ARG(h != nullptr, "null handle");
-  PF_CHECK_ARG(variant >= PF_VARIANT_AUTO && variant <= PF_VARIANT_WARPSPLIT && variant != 7,
+  PF_CHECK_ARG(variant >= PF_VARIANT_AUTO && variant <= PF_VARIANT_WARPSPLIT && variant != 6,
                "unknown variant %d", variant);
   h->variant = variant;
   return PF_OK;

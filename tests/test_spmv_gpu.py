@@ -72,7 +72,7 @@ def check(oracle, y, rp, col, val, x, vdt, alpha=1.0, beta=0.0, y0=None):
 
 
 VARIANTS = {"auto": 0, "nnzsplit": 1, "rowgroup": 2, "nnzsplit_ldg": 3, "rowvec": 4,
-            "rowvec_lx": 5, "nnztile": 6, "warpsplit": 8}
+            "rowvec_lx": 5, "nnzrow": 7, "warpsplit": 8}
 
 
 @pytest.fixture
@@ -94,7 +94,7 @@ def test_cases_variants(pf, oracle, torch_cuda, variant_handle, name, vdt, idt):
     check(oracle, y, rp, col, val, x, vdt)
 
 
-@pytest.mark.parametrize("variant_handle", ["nnzsplit", "nnzsplit_ldg", "nnztile", "warpsplit"],
+@pytest.mark.parametrize("variant_handle", ["nnzsplit", "nnzsplit_ldg", "nnzrow", "warpsplit"],
                          indirect=True)
 @pytest.mark.parametrize("name", ["tiny", "row0_long", "empty_edges", "powerlaw", "mixed_long"])
 @pytest.mark.parametrize("slice_nnz", [1, 3, 7, 64, 1000, 5000])
@@ -108,7 +108,7 @@ def test_small_slices_force_cut_rows(pf, oracle, torch_cuda, variant_handle, nam
 
 
 @pytest.mark.parametrize("variant_handle", ["nnzsplit", "rowgroup", "rowvec", "rowvec_lx",
-                                            "nnztile", "warpsplit"],
+                                            "nnzrow", "warpsplit"],
                          indirect=True)
 @pytest.mark.parametrize("offset", [1, 2, 3, 5])
 def test_unaligned_array_starts(pf, oracle, torch_cuda, variant_handle, offset):
