@@ -437,7 +437,7 @@ def main():
                          "kernel: per-config single-GPU multiply timing")
     ap.add_argument("--config", default="1,2,3,4,5", help="kernel mode: configs")
     ap.add_argument("--dtype", default="f64", help="kernel mode: f64, f32, f16, bf16 (comma list)")
-    ap.add_argument("--variant", type=int, default=0, help="kernel mode: 0 auto, 1-4 forced")
+    ap.add_argument("--variant", type=int, default=0, help="kernel mode: 0 auto, or a forced pf_variant (1, 2, 4, 7)")
     ap.add_argument("--rows", type=int, default=0,
                     help="override m (kernel mode; power mode: profiling slice of config 5)")
     ap.add_argument("--cols", type=int, default=0, help="kernel mode: override n")

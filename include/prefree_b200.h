@@ -40,17 +40,15 @@ typedef enum pf_status {
   PF_ERR_FORMAT = 6       /* Matrix Market text could not be parsed         */
 } pf_status;
 
-/* Kernel variants (compile-time table, selected per call; AUTO = selector). */
+/* Kernel variants (compile-time table, selected per call; AUTO = selector).
+ * The missing numbers belonged to variants that measured slower on every
+ * configuration and were removed; forcing them is refused. */
 typedef enum pf_variant {
   PF_VARIANT_AUTO = 0,
-  PF_VARIANT_NNZSPLIT = 1, /* nnz-balanced CTA slices, any row length        */
-  PF_VARIANT_ROWGROUP = 2, /* row-aligned slices, warp lanes per row (short) */
-  PF_VARIANT_NNZSPLIT_LDG = 3, /* NNZSPLIT with plain coalesced loads (no TMA) */
-  PF_VARIANT_ROWVEC = 4,   /* row-aligned, 16-byte block loads per lane        */
-  PF_VARIANT_ROWVEC_LX = 5, /* ROWVEC + long rows finished in balanced chunks  */
-  /* 6 is unused (measured slower everywhere and removed) */
-  PF_VARIANT_NNZROW = 7,   /* nnz slices, products in shared memory, row pieces summed */
-  PF_VARIANT_WARPSPLIT = 8  /* nnz-balanced slices per warp, any row length     */
+  PF_VARIANT_NNZSPLIT = 1, /* nnz slices streamed by bulk copies (the no-alloc kernel) */
+  PF_VARIANT_ROWGROUP = 2, /* row groups, scalar loads: unaligned col/val    */
+  PF_VARIANT_ROWVEC = 4,   /* row groups, 16-byte block loads: regular rows    */
+  PF_VARIANT_NNZROW = 7    /* nnz slices, row pieces summed: irregular rows   */
 } pf_variant;
 
 typedef struct pf_handle_s *pf_handle;

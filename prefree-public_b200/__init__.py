@@ -25,11 +25,8 @@ LIB_PATH = os.path.join(_HERE, "libprefree_b200.so")
 PF_OK = 0
 STATUS_NAMES = {0: "PF_OK", 1: "PF_ERR_INVALID", 2: "PF_ERR_CUDA", 3: "PF_ERR_DEVICE",
                 4: "PF_ERR_UNSUPPORTED", 5: "PF_ERR_IO", 6: "PF_ERR_FORMAT"}
-(VARIANT_AUTO, VARIANT_NNZSPLIT, VARIANT_ROWGROUP, VARIANT_NNZSPLIT_LDG, VARIANT_ROWVEC,
- VARIANT_ROWVEC_LX) = range(6)
-VARIANT_NNZROW, VARIANT_WARPSPLIT = 7, 8  # 6 is unused
-VARIANT_NAMES = ["auto", "nnzsplit", "rowgroup", "nnzsplit_ldg", "rowvec", "rowvec_lx",
-                 "unused6", "nnzrow", "warpsplit"]
+VARIANT_AUTO, VARIANT_NNZSPLIT, VARIANT_ROWGROUP, VARIANT_ROWVEC, VARIANT_NNZROW = 0, 1, 2, 4, 7
+VARIANT_NAMES = {0: "auto", 1: "nnzsplit", 2: "rowgroup", 4: "rowvec", 7: "nnzrow"}
 
 # every extern "C" symbol include/*.h declares (checked by the CPU tests)
 EXPORTED = [

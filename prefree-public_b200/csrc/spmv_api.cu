@@ -13,7 +13,6 @@
 #include "spmv_rowgroup.cuh"
 #include "spmv_rowvec.cuh"
 #include "spmv_tma.cuh"
-#include "spmv_warpsplit.cuh"
 #include "spmm_rowvec.cuh"
 
 namespace pf {
@@ -66,25 +65,19 @@ struct pf_handle_s {
   int cache_n = 0, cache_next = 0;
   int64_t *sample_dev = nullptr;
   int64_t *sample_host = nullptr;  // pinned
-  int64_t slice_override = 0;  // testing knob: fixed nnz per slice (NNZSPLIT*, WARPSPLIT)
+  int64_t slice_override = 0;  // testing knob: fixed nnz per slice (NNZSPLIT, NNZROW)
   // cut-row scratch
   double *carry = nullptr;     // 2 * cap doubles (head, tail)
   unsigned *counters = nullptr;
   int64_t cap = 0;
   bool scratch_dirty = false;
   unsigned *err = nullptr;
-  // long-row chunk descriptors (ROWVEC_LX), one allocation,
-  // counters zeroed when grown
-  void *lx_buf = nullptr;
-  size_t lx_bytes = 0;
-  bool lx_dirty = false;
   // fused all-gather: per-CTA norm partials + counter (zeroed when grown)
   double *dist_part = nullptr;
   unsigned *dist_counter = nullptr;
   unsigned long long *dist_wait = nullptr;  // step-barrier wait, ns summed over CTAs
   int64_t dist_grid = 0;                    // CTAs of the last fused launch
   int64_t dist_cap = 0;
-  pf::LongRowScratch lx{};
   // host-call buffers
   void *hbuf[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
   size_t hcap[5] = {0, 0, 0, 0, 0};
@@ -110,64 +103,6 @@ static pf_status ensure_scratch(pf_handle h, int64_t num_ctas, cudaStream_t st) 
     h->scratch_dirty = false;
   }
   return PF_OK;
-}
-
-// non-zeros per long-row chunk: the window spmv_longrow_chunks_kernel covers
-// in one pass (128 * its UNR)
-constexpr int64_t kLxChunk = 512;
-
-static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
-
-// Chunk descriptors sized for the worst case of this nnz: at most nnz/(lt+1)
-// rows are longer than lt, and they hold at most nnz/chunk + that many chunks.
-static pf_status ensure_lx(pf_handle h, int64_t nnz, int64_t lt, int64_t chunk, cudaStream_t st) {
-  const int64_t cc = ceil_div(nnz, chunk) + nnz / (lt + 1) + 1;
-  if (cc <= h->lx.cap_chunks && !h->lx_dirty) return PF_OK;
-  const int64_t cap = std::max(cc, h->lx.cap_chunks);
-  const size_t b_hdr = 256;
-  const size_t b_desc = align256(sizeof(LongChunk) * (size_t)cap);
-  const size_t b_cnt = align256(sizeof(unsigned) * (size_t)cap);
-  const size_t b_part = align256(sizeof(double) * (size_t)cap);
-  const size_t total = b_hdr + b_desc + b_cnt + b_part;
-  if (total > h->lx_bytes) {
-    if (h->lx_buf) cudaFree(h->lx_buf);
-    h->lx_buf = nullptr;
-    h->lx_bytes = 0;
-    PF_CUDA_TRY(cudaMalloc(&h->lx_buf, total));
-    h->lx_bytes = total;
-  }
-  char *b = (char *)h->lx_buf;
-  h->lx.alloc = (unsigned long long *)b;
-  h->lx.done = (unsigned *)(b + 8);
-  h->lx.chunks = (LongChunk *)(b + b_hdr);
-  h->lx.cnt = (unsigned *)(b + b_hdr + b_desc);
-  h->lx.part = (double *)(b + b_hdr + b_desc + b_cnt);
-  h->lx.cap_chunks = cap;
-  // counters start at zero (afterwards the kernels leave them at zero)
-  PF_CUDA_TRY(cudaMemsetAsync(h->lx_buf, 0, b_hdr, st));
-  PF_CUDA_TRY(cudaMemsetAsync(h->lx.cnt, 0, b_cnt, st));
-  h->lx_dirty = false;
-  return PF_OK;
-}
-
-template <typename VT, typename IT>
-struct NnzSplitCfg {
-  static constexpr int NT = 256;
-  static constexpr int K = 7;
-  static constexpr int W = 512;
-};
-
-template <typename VT, typename IT>
-static int nnzsplit_occupancy() {
-  using C = NnzSplitCfg<VT, IT>;
-  static int occ = -1;
-  if (occ < 0) {
-    int o = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-        &o, spmv_nnzsplit_kernel<VT, IT, C::NT, C::K, C::W>, C::NT, 0);
-    occ = std::max(1, o);
-  }
-  return occ;
 }
 
 // Kernels with more than 48 KB of dynamic shared memory need the attribute
@@ -228,8 +163,9 @@ static pf_variant_choice choose_from_stats(int64_t m, int64_t nnz, const int64_t
   pf_variant_choice ch;
   // regular rows (the sample never strays far above the mean): whole rows per
   // lane group. Otherwise equal-nnz slices per CTA (NNZROW): on the power-law
-  // config 196 us against 216 for the per-warp slices of WARPSPLIT and ~430
-  // for ROWVEC_LX, whose row kernel waits on each step's longest short row.
+  // config 196 us against 216 for per-warp slices walked from a row_ptr
+  // window and ~430 for row groups with long rows split off, whose row
+  // kernel waits on each step's longest short row.
   if (mx <= 4.0 * avg + 32.0) {
     ch.variant = PF_VARIANT_ROWVEC;
     ch.lanes = rowvec_lanes(avg);
@@ -254,8 +190,8 @@ static pf_status select_variant(pf_handle h, int64_t m, int64_t nnz, const IT *r
                                 cudaStream_t st, pf_variant_choice *out) {
   if (h->variant != PF_VARIANT_AUTO) {
     const double avg = m > 0 ? (double)nnz / (double)m : 0.0;
-    const bool rv = h->variant == PF_VARIANT_ROWVEC || h->variant == PF_VARIANT_ROWVEC_LX;
-    *out = pf_variant_choice{h->variant, rv ? rowvec_lanes(avg) : rowgroup_lanes(avg)};
+    *out = pf_variant_choice{h->variant, h->variant == PF_VARIANT_ROWVEC ? rowvec_lanes(avg)
+                                                                          : rowgroup_lanes(avg)};
     return PF_OK;
   }
   for (int i = 0; i < h->cache_n; ++i) {
@@ -285,25 +221,9 @@ static pf_status select_variant(pf_handle h, int64_t m, int64_t nnz, const IT *r
 }
 
 template <typename VT, typename IT>
-static pf_status launch_warpsplit(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st);
-template <typename VT, typename IT>
 static pf_status launch_nnzrow(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st);
-
-// The long-row chunk kernel: a full wave of resident CTAs (warps stride
-// over the chunk list, so more CTAs only add waves of idle warps).
 template <typename VT, typename IT>
-static void launch_chunks(pf_handle h, const SpmvParams<VT, IT> &prm, cudaStream_t st) {
-  constexpr int NTB = 256;
-  static int occ = -1;
-  if (occ < 0) {
-    int o = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, spmv_longrow_chunks_kernel<VT, IT, NTB>,
-                                                  NTB, 0);
-    occ = std::max(1, o);
-  }
-  spmv_longrow_chunks_kernel<VT, IT, NTB>
-      <<<(unsigned)(h->num_sms * occ), NTB, 0, st>>>(prm, h->lx);
-}
+static pf_status launch_nnzsplit_tma(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st);
 
 template <typename VT, typename IT, int V>
 static pf_status launch_rowgroup(pf_handle h, const SpmvParams<VT, IT> &prm, cudaStream_t st) {
@@ -319,8 +239,7 @@ static pf_status launch_rowgroup(pf_handle h, const SpmvParams<VT, IT> &prm, cud
 }
 
 template <typename VT, typename IT, int V>
-static pf_status launch_rowvec(pf_handle h, const SpmvParams<VT, IT> &prm, bool lx,
-                               cudaStream_t st) {
+static pf_status launch_rowvec(pf_handle h, const SpmvParams<VT, IT> &prm, cudaStream_t st) {
   // U = 2 rows per lane group in flight, built for 4 CTAs per SM (64
   // registers): the best of a sweep over V, U and the CTA bound on configs
   // 1, 2, 4 and 5
@@ -329,20 +248,8 @@ static pf_status launch_rowvec(pf_handle h, const SpmvParams<VT, IT> &prm, bool 
   const int64_t want = ceil_div(prm.m, rows_per_block);
   const int64_t cap = (int64_t)h->num_sms * 16;
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min(want, cap));
-  if (!lx) {
-    spmv_rowvec_kernel<VT, IT, V, U, NTB, false, MINB>
-        <<<grid, NTB, 0, st>>>(prm, LongRowScratch{}, INT64_MAX, kLxChunk);
-    count_launch();
-    PF_CUDA_TRY(cudaGetLastError());
-    return PF_OK;
-  }
-  // rows longer than four block-steps of the group go to the chunk kernel
-  const int64_t lt = 16 * V;
-  pf_status s = ensure_lx(h, prm.nnz, lt, kLxChunk, st);
-  if (s != PF_OK) return s;
-  spmv_rowvec_kernel<VT, IT, V, U, NTB, true, MINB><<<grid, NTB, 0, st>>>(prm, h->lx, lt, kLxChunk);
-  launch_chunks<VT, IT>(h, prm, st);
-  count_launch(2);
+  spmv_rowvec_kernel<VT, IT, V, U, NTB, MINB><<<grid, NTB, 0, st>>>(prm);
+  count_launch();
   PF_CUDA_TRY(cudaGetLastError());
   return PF_OK;
 }
@@ -371,8 +278,7 @@ static pf_status launch_rowvec_dist(pf_handle h, const SpmvParams<double, IT> &p
   d.counter = h->dist_counter;
   d.wait_ns = h->dist_wait;
   h->dist_grid = grid;
-  spmv_rowvec_kernel<double, IT, V, U, NTB, false, MINB, true>
-      <<<(unsigned)grid, NTB, 0, st>>>(prm, LongRowScratch{}, INT64_MAX, kLxChunk, d);
+  spmv_rowvec_kernel<double, IT, V, U, NTB, MINB, true><<<(unsigned)grid, NTB, 0, st>>>(prm, d);
   count_launch();
   PF_CUDA_TRY(cudaGetLastError());
   return PF_OK;
@@ -461,13 +367,7 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
   pf_variant_choice ch;
   pf_status s = select_variant<IT>(h, m, nnz, row_ptr, st, &ch);
   if (s != PF_OK) return s;
-  constexpr bool kHalf = sizeof(VT) == 2;
   ch = for_values(h, ch, (int)sizeof(VT));
-  if (kHalf) {
-    // 16-bit values run on the row-vector, warp-slice and plain-load kernels
-    const double avg = (double)nnz / (double)m;
-    if (ch.variant == PF_VARIANT_NNZSPLIT) ch.variant = PF_VARIANT_NNZSPLIT_LDG;
-  }
 
   SpmvParams<VT, IT> prm;
   prm.m = m;
@@ -481,116 +381,56 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
   prm.alpha = alpha;
   prm.beta = beta;
   prm.err = h->err;
+  prm.T = 0;
+  prm.num_ctas = 0;
+  prm.carry_head = prm.carry_tail = nullptr;
+  prm.counters = nullptr;
 
+  const bool aligned = (((uintptr_t)col | (uintptr_t)val) & 15) == 0;
+  // NNZSPLIT (bulk copies) takes fp32/fp64 values on 16-byte aligned
+  // col/val; NNZROW, which takes any, otherwise
+  if (ch.variant == PF_VARIANT_NNZSPLIT) {
+    if constexpr (sizeof(VT) >= 4) {
+      if (aligned) return launch_nnzsplit_tma<VT, IT>(h, prm, st);
+    }
+    ch.variant = PF_VARIANT_NNZROW;
+  }
   if (ch.variant == PF_VARIANT_NNZROW) return launch_nnzrow<VT, IT>(h, prm, st);
-  // WARPSPLIT needs 16-byte aligned col/val (16-byte block loads)
-  if (ch.variant == PF_VARIANT_WARPSPLIT) {
-    if ((((uintptr_t)col | (uintptr_t)val) & 15) == 0) return launch_warpsplit<VT, IT>(h, prm, st);
-    ch.variant = PF_VARIANT_NNZSPLIT_LDG;
-  }
-  // ROWVEC needs 16-byte aligned col/val (16-byte block loads)
-  if (ch.variant == PF_VARIANT_ROWVEC_LX && (((uintptr_t)col | (uintptr_t)val) & 15) != 0) {
-    ch.variant = PF_VARIANT_NNZSPLIT_LDG;  // irregular rows, unaligned arrays
-  }
-  if (ch.variant == PF_VARIANT_ROWVEC &&
-      (((uintptr_t)col | (uintptr_t)val) & 15) != 0) {
+  // ROWVEC needs 16-byte aligned col/val (16-byte block loads); ROWGROUP,
+  // its scalar-load form, otherwise
+  if (ch.variant == PF_VARIANT_ROWVEC && !aligned) {
     ch.variant = PF_VARIANT_ROWGROUP;
     ch.lanes = rowgroup_lanes(m > 0 ? (double)nnz / (double)m : 0.0);
   }
-  if (ch.variant == PF_VARIANT_ROWVEC || ch.variant == PF_VARIANT_ROWVEC_LX) {
-    const bool lx = ch.variant == PF_VARIANT_ROWVEC_LX;
-    prm.T = 0;
-    prm.num_ctas = 0;
-    prm.carry_head = prm.carry_tail = nullptr;
-    prm.counters = nullptr;
+  if (ch.variant == PF_VARIANT_ROWVEC) {
     switch (ch.lanes) {
-      case 2: return launch_rowvec<VT, IT, 2>(h, prm, lx, st);
-      case 4: return launch_rowvec<VT, IT, 4>(h, prm, lx, st);
-      case 8: return launch_rowvec<VT, IT, 8>(h, prm, lx, st);
-      case 16: return launch_rowvec<VT, IT, 16>(h, prm, lx, st);
-      default: return launch_rowvec<VT, IT, 32>(h, prm, lx, st);
+      case 2: return launch_rowvec<VT, IT, 2>(h, prm, st);
+      case 4: return launch_rowvec<VT, IT, 4>(h, prm, st);
+      case 8: return launch_rowvec<VT, IT, 8>(h, prm, st);
+      case 16: return launch_rowvec<VT, IT, 16>(h, prm, st);
+      default: return launch_rowvec<VT, IT, 32>(h, prm, st);
     }
   }
-  if (ch.variant == PF_VARIANT_ROWGROUP) {
-    prm.T = 0;
-    prm.num_ctas = 0;
-    prm.carry_head = prm.carry_tail = nullptr;
-    prm.counters = nullptr;
-    switch (ch.lanes) {
-      case 4: return launch_rowgroup<VT, IT, 4>(h, prm, st);
-      case 8: return launch_rowgroup<VT, IT, 8>(h, prm, st);
-      case 16: return launch_rowgroup<VT, IT, 16>(h, prm, st);
-      default: return launch_rowgroup<VT, IT, 32>(h, prm, st);
-    }
+  switch (ch.lanes) {  // ROWGROUP
+    case 4: return launch_rowgroup<VT, IT, 4>(h, prm, st);
+    case 8: return launch_rowgroup<VT, IT, 8>(h, prm, st);
+    case 16: return launch_rowgroup<VT, IT, 16>(h, prm, st);
+    default: return launch_rowgroup<VT, IT, 32>(h, prm, st);
   }
-
-  const bool tma = !kHalf && (ch.variant == PF_VARIANT_NNZSPLIT);
-  size_t smem = 0;
-  int64_t T, min_T;
-  int occ;
-  if constexpr (!kHalf) {
-    if (tma) {
-      occ = tma_occupancy<VT, IT>(h->device, &smem);
-      min_T = 2 * TmaCfgDefault::TILE;
-    }
-  }
-  if (!tma) {
-    occ = nnzsplit_occupancy<VT, IT>();
-    min_T = NnzSplitCfg<VT, IT>::NT * NnzSplitCfg<VT, IT>::K;
-  }
-  if (h->slice_override > 0) {
-    T = h->slice_override;
-  } else {
-    const int64_t ctas = (int64_t)h->num_sms * occ;
-    T = std::max<int64_t>(ceil_div(nnz, ctas), min_T);
-  }
-  const int64_t P = ceil_div(nnz, T);
-  PF_CHECK_ARG(P <= INT32_MAX, "too many CTA slices");
-  s = ensure_scratch(h, P, st);
-  if (s != PF_OK) return s;
-  prm.T = T;
-  prm.num_ctas = P;
-  prm.carry_head = h->carry;
-  prm.carry_tail = h->carry + h->cap;
-  prm.counters = h->counters;
-  if constexpr (!kHalf) {
-    if (tma) {
-      using C = TmaCfgDefault;
-      spmv_tma_kernel<VT, IT, C><<<(unsigned)P, C::NT, smem, st>>>(prm);
-    }
-  }
-  if (!tma) {
-    using C = NnzSplitCfg<VT, IT>;
-    spmv_nnzsplit_kernel<VT, IT, C::NT, C::K, C::W><<<(unsigned)P, C::NT, 0, st>>>(prm);
-  }
-  count_launch();
-  PF_CUDA_TRY(cudaGetLastError());
-  return PF_OK;
 }
 
-// WARPSPLIT: one wave of resident CTAs, one equal-nnz slice per warp (at
-// least one tile each).
+// NNZSPLIT: one CTA per equal-nnz slice, one wave of resident CTAs; a
+// producer warp streams the slice with bulk copies (spmv_tma.cuh).
 template <typename VT, typename IT>
-static pf_status launch_warpsplit(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st) {
-  // row_ptr window, ring stages, CTAs per SM, non-zeros per lane: the best
-  // of sweeps on the configs
-  constexpr int NTB = 256, WIN = 128, NS = 2, MINB = 3, EPL = 8;
-  auto kern = spmv_warpsplit_kernel<VT, IT, NTB, WIN, NS, MINB, EPL>;
-  const size_t smem = sizeof(WarpSplitSmem<VT, WIN, NS, EPL>) * (NTB / 32);
-  static int occ_dev[kMaxDevices] = {};
-  int &occ = occ_dev[h->device % kMaxDevices];
-  if (occ == 0) {
-    PF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    int o = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, NTB, smem);
-    occ = std::max(1, o);
-  }
-  const int64_t warps = (int64_t)h->num_sms * occ * (NTB / 32);
-  const int64_t T = h->slice_override > 0 ? h->slice_override
-                                          : std::max<int64_t>(ceil_div(prm.nnz, warps), 32 * EPL);
+static pf_status launch_nnzsplit_tma(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st) {
+  size_t smem = 0;
+  const int occ = tma_occupancy<VT, IT>(h->device, &smem);
+  const int64_t T = h->slice_override > 0
+                        ? h->slice_override
+                        : std::max<int64_t>(ceil_div(prm.nnz, (int64_t)h->num_sms * occ),
+                                            2 * TmaCfgDefault::TILE);
   const int64_t P = ceil_div(prm.nnz, T);
-  PF_CHECK_ARG(P <= INT32_MAX, "too many slices");
-  PF_CHECK_ARG(T < INT32_MAX, "slice too long");
+  PF_CHECK_ARG(P <= INT32_MAX, "too many CTA slices");
   pf_status s = ensure_scratch(h, P, st);
   if (s != PF_OK) return s;
   prm.T = T;
@@ -598,8 +438,8 @@ static pf_status launch_warpsplit(pf_handle h, SpmvParams<VT, IT> prm, cudaStrea
   prm.carry_head = h->carry;
   prm.carry_tail = h->carry + h->cap;
   prm.counters = h->counters;
-  const int64_t grid = std::min<int64_t>(ceil_div(P, NTB / 32), (int64_t)h->num_sms * occ);
-  kern<<<(unsigned)grid, NTB, smem, st>>>(prm);
+  using C = TmaCfgDefault;
+  spmv_tma_kernel<VT, IT, C><<<(unsigned)P, C::NT, smem, st>>>(prm);
   count_launch();
   PF_CUDA_TRY(cudaGetLastError());
   return PF_OK;
@@ -848,7 +688,6 @@ pf_status pf_handle_destroy(pf_handle h) {
   if (h->err) cudaFree(h->err);
   for (int i = 0; i < 5; ++i)
     if (h->hbuf[i]) cudaFree(h->hbuf[i]);
-  if (h->lx_buf) cudaFree(h->lx_buf);
   if (h->dist_part) cudaFree(h->dist_part);
   if (h->sample_dev) cudaFree(h->sample_dev);
   if (h->sample_host) cudaFreeHost(h->sample_host);
@@ -859,7 +698,9 @@ pf_status pf_handle_destroy(pf_handle h) {
 
 pf_status pf_handle_set_variant(pf_handle h, int variant) {
   PF_CHECK_ARG(h != nullptr, "null handle");
-  PF_CHECK_ARG(variant >= PF_VARIANT_AUTO && variant <= PF_VARIANT_WARPSPLIT && variant != 6,
+  PF_CHECK_ARG(variant == PF_VARIANT_AUTO || variant == PF_VARIANT_NNZSPLIT ||
+                   variant == PF_VARIANT_ROWGROUP || variant == PF_VARIANT_ROWVEC ||
+                   variant == PF_VARIANT_NNZROW,
                "unknown variant %d", variant);
   h->variant = variant;
   return PF_OK;
@@ -881,7 +722,6 @@ pf_status pf_handle_device_error(pf_handle h, uint32_t *bits, int clear) {
   if (clear && v) {
     PF_CUDA_TRY(cudaMemset(h->err, 0, sizeof(unsigned)));
     h->scratch_dirty = true;  // a failed launch may leave counters set
-    h->lx_dirty = true;
   }
   return PF_OK;
 }

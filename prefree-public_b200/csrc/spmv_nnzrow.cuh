@@ -12,7 +12,8 @@
 //      the column and value elements it loaded during the previous tile, and
 //      parks them in shared memory; it then loads the next tile's elements
 //      (coalesced warp loads, in flight while this tile is summed);
-//   2. thread j takes row r_cur + done + j of the window of NT rows: the
+//   2. thread j takes row r_cur + done + j of the window of NT rows (the
+//      first window's bounds are loaded with the tile's x gathers): the
 //      row's piece of the tile is [max(start, tb), min(end, te)). A piece of
 //      at most LS products is summed by the thread itself; longer pieces are
 //      listed and summed afterwards by a warp each (lane-strided, then
@@ -129,6 +130,11 @@ spmv_nnzrow_kernel(const SpmvParams<VT, IT> P) {
     const int par = i & 1;
     const int tb = i * TILE;
     const int te = min(tb + TILE, L);
+    // the bounds of the first window's rows, loaded with the x gathers
+    int64_t R = r_cur + tid;
+    bool have = R < P.m;
+    int rs = have ? rel(R) : L + 1;
+    int re = have ? rel(R + 1) : L + 1;
     // ---- 1. products of this tile, then the next tile's loads
     {
       VT xv[K];
@@ -153,10 +159,6 @@ spmv_nnzrow_kernel(const SpmvParams<VT, IT> P) {
     // ---- 2. rows of the tile, window by window
     int done = 0;
     while (true) {
-      const int64_t R = r_cur + done + tid;
-      const bool have = R < P.m;
-      const int rs = have ? rel(R) : L + 1;
-      const int re = have ? rel(R + 1) : L + 1;
       // an empty row that starts at S1 belongs to the next slice (the last
       // slice takes every row)
       const bool fin = have && re <= te && !(!last && re == rs && rs == L);
@@ -178,6 +180,11 @@ spmv_nnzrow_kernel(const SpmvParams<VT, IT> P) {
       const int nf = __syncthreads_count(fin);
       done += nf;
       if (nf < NT) break;
+      // every row of the window ends in this tile: the next window
+      R = r_cur + done + tid;
+      have = R < P.m;
+      rs = have ? rel(R) : L + 1;
+      re = have ? rel(R + 1) : L + 1;
     }
     // ---- 3. long pieces, one warp each
     const int nlong = min(s_nlong[par], LCAP);

@@ -71,13 +71,6 @@ struct Block4<float> {
   }
 };
 
-// LX (long-row escape): a row longer than `lt` non-zeros is not summed here;
-// lane 0 of its group appends it to the CTA's list in shared memory, and at
-// the end the CTA reserves chunk ids for its whole list with one global
-// atomic and writes the chunk descriptors; spmv_longrow_chunks_kernel sums
-// them. (One global atomic per long row, all on one address, serialises: on a
-// power-law matrix with 40k long rows it cost ~150 us.) Rows beyond the
-// shared list's capacity are published one by one.
 // DIST: the fused all-gather epilogue of DistOut (fp64 only).
 // ||y||^2 of the CTA in a fixed order (warp shuffles, then warps in order),
 // one partial per CTA; the last CTA to finish sums the partials in CTA order
@@ -125,49 +118,9 @@ __device__ __forceinline__ void dist_norm_epilogue(const DistOut &D, double nsq)
   __threadfence_system();
 }
 
-// Publishes a CTA's shared list of long rows (called by every thread): one
-// global atomic reserves chunk ids for the whole list, in list order, then
-// warp 0 writes the chunk descriptors.
-__device__ __forceinline__ void lx_publish_list(const LongRowScratch &L, const int64_t (*lst)[3],
-                                                const unsigned *n_shared, int cap, int64_t chunk,
-                                                unsigned *err) {
-  __syncthreads();
-  const unsigned cnt = min(*n_shared, (unsigned)cap);
-  if (cnt == 0 || threadIdx.x >= 32) return;
-  const int lane = threadIdx.x;
-  int64_t tot = 0;
-  for (unsigned i = lane; i < cnt; i += 32) tot += lx_num_chunks(lst[i][1], lst[i][2], chunk);
-#pragma unroll
-  for (int d = 16; d > 0; d >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, d);
-  int64_t off = 0;
-  if (lane == 0) off = (int64_t)atomicAdd(L.alloc, (unsigned long long)tot);
-  off = __shfl_sync(0xffffffffu, off, 0);
-  if (off + tot > L.cap_chunks) {
-    if (lane == 0) atomicOr(err, PF_DEVERR_ROWPTR);
-    return;
-  }
-  for (unsigned i0 = 0; i0 < cnt; i0 += 32) {
-    const unsigned i = i0 + lane;
-    const int64_t nch = i < cnt ? lx_num_chunks(lst[i][1], lst[i][2], chunk) : 0;
-    int64_t inc = nch;  // inclusive scan over the batch
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const int64_t t = __shfl_up_sync(0xffffffffu, inc, d);
-      if (lane >= d) inc += t;
-    }
-    const int64_t first = off + inc - nch;
-    for (unsigned j = 0; j < 32 && i0 + j < cnt; ++j) {
-      const int64_t fj = __shfl_sync(0xffffffffu, first, j);
-      lx_write_chunks(L, lst[i0 + j][0], lst[i0 + j][1], lst[i0 + j][2], fj, chunk, lane, 32);
-    }
-    off += __shfl_sync(0xffffffffu, inc, 31);
-  }
-}
-
-template <typename VT, typename IT, int V, int U, int NTB, bool LX, int MINB = 1, bool DIST = false>
+template <typename VT, typename IT, int V, int U, int NTB, int MINB = 1, bool DIST = false>
 __global__ void __launch_bounds__(NTB, MINB)
-spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t lt,
-                   int64_t chunk, const DistOut D = DistOut{}) {
+spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const DistOut D = DistOut{}) {
   constexpr int GPW = 32 / V;  // row groups per warp
   constexpr int64_t RPW = (int64_t)GPW * U;
   // DIST: a warp takes KS consecutive steps over 32 consecutive rows (a
@@ -196,11 +149,6 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
   double nsq = 0.0;  // DIST: this thread's share of ||y||^2
   // DIST: the ranks' next-x pointers, read once per CTA (a row store must not
   // wait on a pointer load)
-  constexpr int LXCAP = LX ? 256 : 1;
-  __shared__ int64_t s_lx[LXCAP][3];  // row, s, e
-  __shared__ unsigned s_lxn;
-  if (LX && threadIdx.x == 0) s_lxn = 0;
-  if (LX) __syncthreads();
   __shared__ double *s_outs[DIST ? 64 : 1];
   __shared__ double s_wbuf[DIST ? NTB / 32 : 1][DIST ? SUPER : 1];  // a warp's super-chunk
   if (DIST) {
@@ -264,21 +212,6 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
     for (int u = 0; u < U; ++u) {
       acc[u] = 0.0;
       skip[u] = false;
-      if (LX && (int64_t)e[u] - (int64_t)s[u] > lt) {
-        skip[u] = true;
-        if (lig == 0) {
-          const int64_t row = rb + (int64_t)u * GPW + gw;
-          const unsigned p = atomicAdd(&s_lxn, 1u);
-          if (p < (unsigned)LXCAP) {
-            s_lx[p][0] = row;
-            s_lx[p][1] = (int64_t)s[u];
-            s_lx[p][2] = (int64_t)e[u];
-          } else {
-            lx_publish_row(L, row, (int64_t)s[u], (int64_t)e[u], chunk, P.err);
-          }
-        }
-        e[u] = s[u];  // nothing to sum here
-      }
       q0[u] = (int64_t)s[u] & ~(int64_t)3;
       lo[u] = (int)((int64_t)s[u] - q0[u]);
       const int64_t l64 = (int64_t)e[u] - q0[u];
@@ -366,101 +299,6 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L, int64_t l
     }
   }
   if (DIST) dist_norm_epilogue<NTB>(D, nsq);
-  if (LX) lx_publish_list(L, s_lx, &s_lxn, LXCAP, chunk, P.err);
-}
-
-// Chunks of the listed long rows: warp w sums chunks w, w + W, ... (W warps in
-// the grid; the next descriptor is loaded while the current chunk is summed).
-// A chunk lies in one aligned window of 128 * UNR non-zeros, which the warp
-// covers in one pass: every lane issues its UNR 16-byte column blocks, value
-// pieces and 4 * UNR x gathers at once. A row of one chunk is written at once;
-// otherwise the chunk stores its partial and the last of the row's chunks to
-// finish sums the partials in chunk order (the same order on every run) and
-// writes y. The last CTA resets the counters.
-template <typename VT, typename IT, int NTB, int UNR = 4>
-__global__ void __launch_bounds__(NTB)
-spmv_longrow_chunks_kernel(const SpmvParams<VT, IT> P, const LongRowScratch L) {
-  constexpr int W = 128 * UNR;  // window = chunk length
-  const int lane = threadIdx.x & 31;
-  const int64_t n_chunks = (int64_t)*((volatile unsigned long long *)L.alloc);
-  const int64_t warp = ((int64_t)blockIdx.x * NTB + threadIdx.x) >> 5;
-  const int64_t nwarps = ((int64_t)gridDim.x * NTB) >> 5;
-  const uint32_t n = (uint32_t)(P.n < 0xffffffffLL ? P.n : 0xffffffffLL);
-  bool bad = false;
-  LongChunk cur;
-  if (warp < n_chunks) cur = L.chunks[warp];
-  for (int64_t g = warp; g < n_chunks; g += nwarps) {
-    LongChunk nxt = cur;
-    if (g + nwarps < n_chunks) nxt = L.chunks[g + nwarps];
-    // offsets inside the chunk's window
-    const int64_t wb = cur.cs & ~(int64_t)(W - 1);
-    const int lo = (int)(cur.cs - wb), hi = lo + cur.len;
-    double acc = 0.0;
-    {
-      int4 c4[UNR];
-      VT v4[UNR][4];
-#pragma unroll
-      for (int j = 0; j < UNR; ++j) {
-        const int q = 4 * lane + 128 * j;
-        const bool act = q < hi && q + 4 > lo;
-        c4[j] = act ? __ldcs(reinterpret_cast<const int4 *>(P.col + wb + q)) : make_int4(0, 0, 0, 0);
-        Block4<VT>::load(P.val + wb, q, act && q + 1 >= lo, act && q + 2 < hi, v4[j]);
-      }
-      VT xv[UNR][4];
-#pragma unroll
-      for (int j = 0; j < UNR; ++j) {
-        const int q = 4 * lane + 128 * j;
-        const int cc[4] = {c4[j].x, c4[j].y, c4[j].z, c4[j].w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const bool use = q + i >= lo && q + i < hi;
-          const bool inb = (uint32_t)cc[i] < n;
-          bad |= use && !inb;
-          xv[j][i] = (use && inb) ? ptx::ldg_x(P.x + cc[i]) : VT(0);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < UNR; ++j) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc += (double)v4[j][i] * (double)xv[j][i];
-      }
-    }
-#pragma unroll
-    for (int d = 16; d > 0; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d);
-    if (lane == 0) {
-      if (cur.nch == 1) {
-        double out = P.alpha * acc;
-        if (P.beta != 0.0) out += P.beta * (double)P.y[cur.row];
-        P.y[cur.row] = (VT)out;
-      } else {
-        L.part[g] = acc;
-        __threadfence();
-        const unsigned old = atomicAdd(&L.cnt[cur.first], 1u);
-        if (old == (unsigned)cur.nch - 1) {
-          __threadfence();
-          double sum = 0.0;
-          for (int c = 0; c < cur.nch; ++c) sum += __ldcg(&L.part[cur.first + c]);
-          double out = P.alpha * sum;
-          if (P.beta != 0.0) out += P.beta * (double)P.y[cur.row];
-          P.y[cur.row] = (VT)out;
-          L.cnt[cur.first] = 0;
-        }
-      }
-    }
-    cur = nxt;
-  }
-  if (bad) atomicOr(P.err, PF_DEVERR_BOUNDS);
-  // last CTA out resets the chunk counter for the next launch
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned old = atomicAdd(L.done, 1u);
-    if (old == gridDim.x - 1) {
-      *L.alloc = 0ull;
-      *L.done = 0;
-      __threadfence();
-    }
-  }
 }
 
 }  // namespace pf

@@ -15,8 +15,7 @@ from csr_cases import case
 
 pytestmark = pytest.mark.gpu
 
-VARIANTS = {"auto": 0, "nnzsplit": 1, "rowgroup": 2, "nnzsplit_ldg": 3, "rowvec": 4,
-            "rowvec_lx": 5, "nnzrow": 7, "warpsplit": 8}
+VARIANTS = {"auto": 0, "nnzsplit": 1, "rowgroup": 2, "rowvec": 4, "nnzrow": 7}
 
 
 def run_half(pf, torch, h, rp, col, val, x, n, tdt, idt, alpha=1.0, beta=0.0, y0=None):

@@ -1,14 +1,15 @@
-"""WARPSPLIT's branch-free walk of whole tiles, against the CPU oracle.
+"""NNZROW at the edges of its tile walk, against the CPU oracle.
 
-A 256-non-zero tile whose row ends are all distinct (no empty row ends inside
-it) is walked from a bit mask of its row ends instead of a search of the
-row_ptr window; ends past the 128-entry window are read from row_ptr itself.
-These matrices put that walk at its edges: tiles that are nothing but
-one-non-zero rows (256 ends in one tile), short rows mixed with empty ones
-(the walk must hand those tiles to the searching pass), and slice lengths that
-are multiples of the tile, so that a slice's cut first row ends inside a tile
-the fast walk takes. Tolerance as in the other parity tests; with integer
-values every sum is exact and the results must be bit-identical.
+A tile is 512 non-zeros of a slice; its rows are taken in windows of 64
+(one per thread), a row piece of more than 64 products goes to a warp, and
+the sum of the row left open at the tile's end is carried to the next tile.
+These matrices put that walk at its edges: long runs of one-non-zero rows
+(512 row ends in one tile: eight windows), short rows mixed with empty ones,
+heavy tails (long pieces next to short ones), and slice lengths around and
+at multiples of the tile, so that a slice's cut first row ends inside a tile
+and cut rows span several slices. Tolerance as in the other parity tests;
+with integer values every sum is exact and the results must be
+bit-identical.
 """
 import numpy as np
 import pytest
@@ -18,7 +19,7 @@ from csr_cases import from_lengths
 pytestmark = pytest.mark.gpu
 
 EPS = {np.float64: 1e-12, np.float32: 1e-5}
-WARPSPLIT = 8
+NNZROW = 7
 
 
 @pytest.fixture(scope="module")
@@ -31,7 +32,7 @@ def torch_cuda():
 @pytest.fixture
 def ws_handle(pf, torch_cuda):
     h = pf.Handle()
-    h.set_variant(WARPSPLIT)
+    h.set_variant(NNZROW)
     yield h
     h.close()
 
@@ -46,7 +47,7 @@ def lengths(name, rng):
             parts.append(rng.integers(300, 3000, size=3))
         return np.concatenate(parts)
     if name == "short_with_empty":
-        # lengths 0-3: many tiles hold an empty row and take the searching pass
+        # lengths 0-3: many empty rows between short ones
         return rng.choice([0, 1, 1, 2, 3], size=40000)
     if name == "short_no_empty":
         return rng.integers(1, 5, size=40000)
@@ -90,9 +91,9 @@ def check(oracle, y, rp, col, val, x, vdt, alpha=1.0, beta=0.0, y0=None):
 
 
 @pytest.mark.parametrize("name", NAMES)
-@pytest.mark.parametrize("slice_nnz", [0, 256, 512, 768, 1000, 4096])
+@pytest.mark.parametrize("slice_nnz", [0, 1, 63, 256, 511, 512, 768, 1000, 4096])
 @pytest.mark.parametrize("idt", [np.int32, np.int64])
-def test_fast_walk_slices(pf, oracle, torch_cuda, ws_handle, name, slice_nnz, idt):
+def test_tile_walk_slices(pf, oracle, torch_cuda, ws_handle, name, slice_nnz, idt):
     rng = np.random.default_rng(11)
     n = 50000
     rp, col, val = from_lengths(rng, lengths(name, rng), n)
@@ -105,7 +106,7 @@ def test_fast_walk_slices(pf, oracle, torch_cuda, ws_handle, name, slice_nnz, id
 @pytest.mark.parametrize("name", NAMES)
 @pytest.mark.parametrize("vdt", [np.float64, np.float32])
 @pytest.mark.parametrize("alpha,beta", [(1.0, 0.0), (-0.75, 0.5), (0.0, 2.0)])
-def test_fast_walk_alpha_beta(pf, oracle, torch_cuda, ws_handle, name, vdt, alpha, beta):
+def test_tile_walk_alpha_beta(pf, oracle, torch_cuda, ws_handle, name, vdt, alpha, beta):
     rng = np.random.default_rng(13)
     n = 50000
     rp, col, val = from_lengths(rng, lengths(name, rng), n)
@@ -118,7 +119,7 @@ def test_fast_walk_alpha_beta(pf, oracle, torch_cuda, ws_handle, name, vdt, alph
 
 @pytest.mark.parametrize("name", NAMES)
 @pytest.mark.parametrize("slice_nnz", [0, 768])
-def test_fast_walk_integer_bit_exact(pf, oracle, torch_cuda, ws_handle, name, slice_nnz):
+def test_tile_walk_integer_bit_exact(pf, oracle, torch_cuda, ws_handle, name, slice_nnz):
     """Integer values and x (the reference harness's i % 15 values): every
     partial sum is exact, so y must equal the serial sum bit for bit."""
     rng = np.random.default_rng(16)

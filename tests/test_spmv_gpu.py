@@ -71,8 +71,7 @@ def check(oracle, y, rp, col, val, x, vdt, alpha=1.0, beta=0.0, y0=None):
     assert ok, f"{nbad} rows out of tolerance (worst ratio {worst:.3g})"
 
 
-VARIANTS = {"auto": 0, "nnzsplit": 1, "rowgroup": 2, "nnzsplit_ldg": 3, "rowvec": 4,
-            "rowvec_lx": 5, "nnzrow": 7, "warpsplit": 8}
+VARIANTS = {"auto": 0, "nnzsplit": 1, "rowgroup": 2, "rowvec": 4, "nnzrow": 7}
 
 
 @pytest.fixture
@@ -94,7 +93,7 @@ def test_cases_variants(pf, oracle, torch_cuda, variant_handle, name, vdt, idt):
     check(oracle, y, rp, col, val, x, vdt)
 
 
-@pytest.mark.parametrize("variant_handle", ["nnzsplit", "nnzsplit_ldg", "nnzrow", "warpsplit"],
+@pytest.mark.parametrize("variant_handle", ["nnzsplit", "nnzrow"],
                          indirect=True)
 @pytest.mark.parametrize("name", ["tiny", "row0_long", "empty_edges", "powerlaw", "mixed_long"])
 @pytest.mark.parametrize("slice_nnz", [1, 3, 7, 64, 1000, 5000])
@@ -107,8 +106,7 @@ def test_small_slices_force_cut_rows(pf, oracle, torch_cuda, variant_handle, nam
     check(oracle, y, rp, col, val, x, np.float64)
 
 
-@pytest.mark.parametrize("variant_handle", ["nnzsplit", "rowgroup", "rowvec", "rowvec_lx",
-                                            "nnzrow", "warpsplit"],
+@pytest.mark.parametrize("variant_handle", ["nnzsplit", "rowgroup", "rowvec", "nnzrow"],
                          indirect=True)
 @pytest.mark.parametrize("offset", [1, 2, 3, 5])
 def test_unaligned_array_starts(pf, oracle, torch_cuda, variant_handle, offset):
