@@ -266,11 +266,21 @@ pf_status pf_prefree_spmv_f32_i32(float *csrVal, int32_t *csrRowPtr,
  * symmetric and Hermitian inputs expanded (off-diagonal entries mirrored),
  * entries of a row kept in file order (no sort), row_ptr has m+1 entries.
  * Differences: 64-bit row_ptr and nnz, a multi-threaded parser, and errors are
- * returned instead of printed. Arrays are malloc'd; free them with pf_free.  */
+ * returned instead of printed. Arrays are malloc'd; free them with pf_free
+ * (pf_mmio_read_pinned below returns page-locked arrays instead).            */
 pf_status pf_mmio_read(const char *path, int64_t *m, int64_t *n, int64_t *nnz,
                        int *is_symmetric, int64_t **row_ptr, int32_t **col_idx,
                        double **val);
 void pf_free(void *p);
+/* pf_mmio_read with the three arrays in page-locked (pinned) host memory, so
+ * that pf_spmv_host_* (or any cudaMemcpyAsync) copies a file-loaded matrix to
+ * the device at full PCIe speed, without a staging copy. Free them with
+ * pf_free, which tells pinned arrays from heap ones. Needs the CUDA runtime
+ * (no device work). No counterpart in the reference, whose mmio_allinone
+ * returns malloc'd arrays (utilities/mmio.cpp:1653-1660). */
+pf_status pf_mmio_read_pinned(const char *path, int64_t *m, int64_t *n, int64_t *nnz,
+                              int *is_symmetric, int64_t **row_ptr, int32_t **col_idx,
+                              double **val);
 
 /* Binary CSR cache: parse a .mtx once, reload its CSR at file-read speed.
  * pf_csr_write / pf_csr_read store and load (m, n, nnz, is_symmetric,
@@ -289,6 +299,12 @@ pf_status pf_csr_read(const char *path, int64_t *m, int64_t *n, int64_t *nnz, in
 pf_status pf_mmio_read_cached(const char *mtx_path, const char *cache_path, int64_t *m,
                               int64_t *n, int64_t *nnz, int *is_symmetric, int64_t **row_ptr,
                               int32_t **col_idx, double **val, int *from_cache);
+/* pf_mmio_read_cached with the arrays in page-locked host memory (as
+ * pf_mmio_read_pinned); free them with pf_free. */
+pf_status pf_mmio_read_cached_pinned(const char *mtx_path, const char *cache_path, int64_t *m,
+                                     int64_t *n, int64_t *nnz, int *is_symmetric,
+                                     int64_t **row_ptr, int32_t **col_idx, double **val,
+                                     int *from_cache);
 
 /* ---- row sharding (multi-GPU) -----------------------------------------------
  * Equal-nnz row split: bounds[k] = first row r with row_ptr[r] - row_ptr[0]

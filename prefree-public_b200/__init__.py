@@ -44,7 +44,8 @@ EXPORTED = [
     "pf_spmv_noalloc_f64_i32", "pf_spmv_dist_f64_i64", "pf_spmv_dist_f64_i32",
     "pf_spmm_f64_i32", "pf_spmm_f64_i64", "pf_spmm_f32_i32", "pf_spmm_f32_i64",
     "pf_spmv_f16_i32", "pf_spmv_f16_i64", "pf_spmv_bf16_i32", "pf_spmv_bf16_i64",
-    "pf_csr_write", "pf_csr_read", "pf_mmio_read_cached",
+    "pf_csr_write", "pf_csr_read", "pf_mmio_read_cached", "pf_mmio_read_pinned",
+    "pf_mmio_read_cached_pinned",
 ]
 # the C++ drop-in symbols of include/PreFree.h (mangled)
 CXX_EXPORTED = [
@@ -118,6 +119,8 @@ def _load():
     lib.pf_csr_write.argtypes = [C.c_char_p, i64, i64, i64, C.c_int, vp, vp, vp]
     lib.pf_csr_read.argtypes = [C.c_char_p] + csr_out
     lib.pf_mmio_read_cached.argtypes = [C.c_char_p, C.c_char_p] + csr_out + [C.POINTER(C.c_int)]
+    lib.pf_mmio_read_cached_pinned.argtypes = lib.pf_mmio_read_cached.argtypes
+    lib.pf_mmio_read_pinned.argtypes = lib.pf_mmio_read.argtypes
     lib.pf_free.argtypes = [vp]
     lib.pf_free.restype = None
     lib.pf_shard_bounds_i32.argtypes = [vp, i64, C.c_int, vp]
@@ -367,11 +370,14 @@ def _csr_out():
             C.c_void_p())
 
 
-def mmio_read(path: str):
+def mmio_read(path: str, pinned: bool = False):
     """Matrix Market -> CSR (mmio_allinone semantics). Returns
-    (m, n, nnz, is_symmetric, row_ptr int64[m+1], col int32[nnz], val f64[nnz])."""
+    (m, n, nnz, is_symmetric, row_ptr int64[m+1], col int32[nnz], val f64[nnz]).
+    pinned: the arrays live in page-locked host memory (full-speed copies to
+    the device, e.g. by spmv_host)."""
     o = _csr_out()
-    _check(lib.pf_mmio_read(os.fsencode(path), *[C.byref(v) for v in o]))
+    f = lib.pf_mmio_read_pinned if pinned else lib.pf_mmio_read
+    _check(f(os.fsencode(path), *[C.byref(v) for v in o]))
     return _take_csr(*o)
 
 
@@ -391,12 +397,13 @@ def csr_read(path: str):
     return _take_csr(*o)
 
 
-def mmio_read_cached(mtx_path: str, cache_path: str):
+def mmio_read_cached(mtx_path: str, cache_path: str, pinned: bool = False):
     """mmio_read through a binary cache: returns (csr tuple, from_cache)."""
     o = _csr_out()
     fc = C.c_int()
-    _check(lib.pf_mmio_read_cached(os.fsencode(mtx_path), os.fsencode(cache_path),
-                                   *[C.byref(v) for v in o], C.byref(fc)))
+    f = lib.pf_mmio_read_cached_pinned if pinned else lib.pf_mmio_read_cached
+    _check(f(os.fsencode(mtx_path), os.fsencode(cache_path), *[C.byref(v) for v in o],
+             C.byref(fc)))
     return _take_csr(*o), bool(fc.value)
 
 

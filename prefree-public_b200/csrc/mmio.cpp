@@ -229,13 +229,37 @@ pf_status shard_bounds(const IT *rp, int64_t m, int parts, int64_t *b) {
 
 }  // namespace
 
+namespace pf {
+// Page-locked host memory for the loader's output arrays (defined in
+// spmv_api.cu, which talks to the CUDA runtime): null on failure; and the
+// free of an array this library returned, pinned or not.
+void *pinned_alloc(size_t bytes);
+bool pinned_free(void *p);  // false: p was not page-locked memory
+}  // namespace pf
+
+namespace {
+// the loader's output arrays: heap (malloc) or page-locked
+void *out_alloc(size_t bytes, bool pinned, bool zero) {
+  void *p = pinned ? pf::pinned_alloc(bytes) : std::malloc(bytes);
+  if (p && zero) std::memset(p, 0, bytes);
+  return p;
+}
+void out_free(void *p, bool pinned) {
+  if (!p) return;
+  if (pinned) pf::pinned_free(p);
+  else std::free(p);
+}
+}  // namespace
+
 extern "C" {
 
-void pf_free(void *p) { std::free(p); }
+void pf_free(void *p) {
+  if (p && !pf::pinned_free(p)) std::free(p);
+}
 
-pf_status pf_mmio_read(const char *path, int64_t *m_out, int64_t *n_out,
-                       int64_t *nnz_out, int *sym_out, int64_t **row_ptr_out,
-                       int32_t **col_out, double **val_out) {
+static pf_status mmio_read_impl(const char *path, int64_t *m_out, int64_t *n_out,
+                                int64_t *nnz_out, int *sym_out, int64_t **row_ptr_out,
+                                int32_t **col_out, double **val_out, bool pinned) {
   if (!path || !m_out || !n_out || !nnz_out || !sym_out || !row_ptr_out || !col_out ||
       !val_out) {
     pf::set_error("pf_mmio_read: null argument");
@@ -395,9 +419,9 @@ pf_status pf_mmio_read(const char *path, int64_t *m_out, int64_t *n_out,
   // each thread owns an equal-nnz range of rows and walks all entries in file
   // order, placing the ones (and the mirrors) that land in its rows, so every
   // row receives its entries in the same order as a single pass would give
-  int64_t *rp = (int64_t *)std::calloc((size_t)M + 1, sizeof(int64_t));
+  int64_t *rp = (int64_t *)out_alloc(sizeof(int64_t) * ((size_t)M + 1), pinned, true);
   if (!rp) {
-    pf::set_error("pf_mmio_read: out of host memory");
+    pf::set_error("pf_mmio_read: out of host memory%s", pinned ? " (page-locked)" : "");
     return PF_ERR_INVALID;
   }
   unsigned ncsr = std::max(1u, std::min(64u, std::thread::hardware_concurrency()));
@@ -418,13 +442,15 @@ pf_status pf_mmio_read(const char *path, int64_t *m_out, int64_t *n_out,
     run += c;
   }
   const int64_t nnz = run;
-  int32_t *col = (int32_t *)std::malloc(sizeof(int32_t) * (size_t)std::max<int64_t>(nnz, 1));
-  double *val = (double *)std::malloc(sizeof(double) * (size_t)std::max<int64_t>(nnz, 1));
+  int32_t *col = (int32_t *)out_alloc(sizeof(int32_t) * (size_t)std::max<int64_t>(nnz, 1), pinned,
+                                      false);
+  double *val = (double *)out_alloc(sizeof(double) * (size_t)std::max<int64_t>(nnz, 1), pinned,
+                                    false);
   if (!col || !val) {
-    std::free(rp);
-    std::free(col);
-    std::free(val);
-    pf::set_error("pf_mmio_read: out of host memory");
+    out_free(rp, pinned);
+    out_free(col, pinned);
+    out_free(val, pinned);
+    pf::set_error("pf_mmio_read: out of host memory%s", pinned ? " (page-locked)" : "");
     return PF_ERR_INVALID;
   }
   // row ranges of equal nnz (thread k owns rows [rb[k], rb[k + 1]))
@@ -519,7 +545,7 @@ static pf_status csr_write(const char *path, int64_t m, int64_t n, int64_t nnz, 
 // match (want_size, want_mtime), else PF_ERR_FORMAT.
 static pf_status csr_read(const char *path, int64_t want_size, int64_t want_mtime, int64_t *m_out,
                           int64_t *n_out, int64_t *nnz_out, int *sym_out, int64_t **rp_out,
-                          int32_t **col_out, double **val_out) {
+                          int32_t **col_out, double **val_out, bool pinned) {
   const int fd = ::open(path, O_RDONLY);
   if (fd < 0) {
     pf::set_error("pf_csr_read: cannot open %s: %s", path, std::strerror(errno));
@@ -537,9 +563,11 @@ static pf_status csr_read(const char *path, int64_t want_size, int64_t want_mtim
     pf::set_error("pf_csr_read: %s is not a matching CSR cache file", path);
     return PF_ERR_FORMAT;
   }
-  int64_t *rp = (int64_t *)std::malloc(sizeof(int64_t) * (size_t)(hd.m + 1));
-  int32_t *col = (int32_t *)std::malloc(sizeof(int32_t) * (size_t)std::max<int64_t>(hd.nnz, 1));
-  double *val = (double *)std::malloc(sizeof(double) * (size_t)std::max<int64_t>(hd.nnz, 1));
+  int64_t *rp = (int64_t *)out_alloc(sizeof(int64_t) * (size_t)(hd.m + 1), pinned, false);
+  int32_t *col =
+      (int32_t *)out_alloc(sizeof(int32_t) * (size_t)std::max<int64_t>(hd.nnz, 1), pinned, false);
+  double *val =
+      (double *)out_alloc(sizeof(double) * (size_t)std::max<int64_t>(hd.nnz, 1), pinned, false);
   const size_t rp_bytes = sizeof(int64_t) * (size_t)(hd.m + 1);
   const size_t col_bytes = sizeof(int32_t) * (size_t)hd.nnz;
   bool ok = rp && col && val && pread_all(fd, (char *)rp, rp_bytes, sizeof(hd)) &&
@@ -570,9 +598,9 @@ static pf_status csr_read(const char *path, int64_t want_size, int64_t want_mtim
     ok = std::all_of(good.begin(), good.end(), [](int v) { return v != 0; });
   }
   if (!ok) {
-    std::free(rp);
-    std::free(col);
-    std::free(val);
+    out_free(rp, pinned);
+    out_free(col, pinned);
+    out_free(val, pinned);
     pf::set_error("pf_csr_read: %s is truncated or inconsistent", path);
     return PF_ERR_FORMAT;
   }
@@ -597,12 +625,13 @@ pf_status pf_csr_read(const char *path, int64_t *m, int64_t *n, int64_t *nnz, in
     pf::set_error("pf_csr_read: null argument");
     return PF_ERR_INVALID;
   }
-  return csr_read(path, -1, 0, m, n, nnz, is_symmetric, row_ptr, col_idx, val);
+  return csr_read(path, -1, 0, m, n, nnz, is_symmetric, row_ptr, col_idx, val, false);
 }
 
-pf_status pf_mmio_read_cached(const char *mtx_path, const char *cache_path, int64_t *m,
-                              int64_t *n, int64_t *nnz, int *is_symmetric, int64_t **row_ptr,
-                              int32_t **col_idx, double **val, int *from_cache) {
+static pf_status mmio_read_cached_impl(const char *mtx_path, const char *cache_path, int64_t *m,
+                                       int64_t *n, int64_t *nnz, int *is_symmetric,
+                                       int64_t **row_ptr, int32_t **col_idx, double **val,
+                                       int *from_cache, bool pinned) {
   if (!mtx_path || !cache_path || !m || !n || !nnz || !is_symmetric || !row_ptr || !col_idx ||
       !val) {
     pf::set_error("pf_mmio_read_cached: null argument");
@@ -614,15 +643,42 @@ pf_status pf_mmio_read_cached(const char *mtx_path, const char *cache_path, int6
     return PF_ERR_IO;
   }
   if (from_cache) *from_cache = 0;
-  if (csr_read(cache_path, sz, mt, m, n, nnz, is_symmetric, row_ptr, col_idx, val) == PF_OK) {
+  if (csr_read(cache_path, sz, mt, m, n, nnz, is_symmetric, row_ptr, col_idx, val, pinned) ==
+      PF_OK) {
     if (from_cache) *from_cache = 1;
     return PF_OK;
   }
-  pf_status st = pf_mmio_read(mtx_path, m, n, nnz, is_symmetric, row_ptr, col_idx, val);
+  pf_status st = mmio_read_impl(mtx_path, m, n, nnz, is_symmetric, row_ptr, col_idx, val, pinned);
   if (st != PF_OK) return st;
   // best effort: a cache that cannot be written only costs the next parse
   csr_write(cache_path, *m, *n, *nnz, *is_symmetric, *row_ptr, *col_idx, *val, sz, mt);
   return PF_OK;
+}
+
+pf_status pf_mmio_read(const char *path, int64_t *m, int64_t *n, int64_t *nnz, int *is_symmetric,
+                       int64_t **row_ptr, int32_t **col_idx, double **val) {
+  return mmio_read_impl(path, m, n, nnz, is_symmetric, row_ptr, col_idx, val, false);
+}
+
+pf_status pf_mmio_read_pinned(const char *path, int64_t *m, int64_t *n, int64_t *nnz,
+                              int *is_symmetric, int64_t **row_ptr, int32_t **col_idx,
+                              double **val) {
+  return mmio_read_impl(path, m, n, nnz, is_symmetric, row_ptr, col_idx, val, true);
+}
+
+pf_status pf_mmio_read_cached(const char *mtx_path, const char *cache_path, int64_t *m,
+                              int64_t *n, int64_t *nnz, int *is_symmetric, int64_t **row_ptr,
+                              int32_t **col_idx, double **val, int *from_cache) {
+  return mmio_read_cached_impl(mtx_path, cache_path, m, n, nnz, is_symmetric, row_ptr, col_idx,
+                               val, from_cache, false);
+}
+
+pf_status pf_mmio_read_cached_pinned(const char *mtx_path, const char *cache_path, int64_t *m,
+                                     int64_t *n, int64_t *nnz, int *is_symmetric,
+                                     int64_t **row_ptr, int32_t **col_idx, double **val,
+                                     int *from_cache) {
+  return mmio_read_cached_impl(mtx_path, cache_path, m, n, nnz, is_symmetric, row_ptr, col_idx,
+                               val, from_cache, true);
 }
 
 pf_status pf_shard_bounds_i32(const int32_t *row_ptr, int64_t m, int parts, int64_t *bounds) {

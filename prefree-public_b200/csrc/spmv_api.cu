@@ -37,6 +37,29 @@ static void count_launch(unsigned long long k = 1) {
 
 void count_launches(unsigned long long k) { count_launch(k); }
 
+// Page-locked host memory for the Matrix Market loader's output (mmio.cpp):
+// host-to-device copies from it run at full PCIe speed with no staging copy.
+void *pinned_alloc(size_t bytes) {
+  void *p = nullptr;
+  if (cudaHostAlloc(&p, bytes > 0 ? bytes : 1, cudaHostAllocDefault) != cudaSuccess) {
+    cudaGetLastError();  // clear the sticky-free error state of the failed call
+    return nullptr;
+  }
+  return p;
+}
+
+// Frees p if it is page-locked memory this process allocated through CUDA;
+// false (nothing done) for any other pointer, which the caller frees itself.
+bool pinned_free(void *p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (a.type != cudaMemoryTypeHost) return false;
+  return cudaFreeHost(p) == cudaSuccess;
+}
+
 }  // namespace pf
 
 // The selector's decision for one matrix.
