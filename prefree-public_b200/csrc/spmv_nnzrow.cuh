@@ -110,9 +110,16 @@ spmv_nnzrow_kernel(const SpmvParams<VT, IT> P) {
   bool bad = false, bad_rows = false;
 
   // a row_ptr entry as a position of the slice, clamped to [-1, L + 1]
+  // (int32 row_ptr: every entry and S0 are below 2^31, so the difference is
+  // exact in 32 bits)
   auto rel = [&](int64_t r) -> int {
-    const int64_t v = (int64_t)__ldg(P.row_ptr + r) - S0;
-    return (int)min(max(v, (int64_t)-1), (int64_t)L + 1);
+    if constexpr (sizeof(IT) == 4) {
+      const int v = (int)__ldg(P.row_ptr + r) - (int)S0;
+      return min(max(v, -1), L + 1);
+    } else {
+      const int64_t v = (int64_t)__ldg(P.row_ptr + r) - S0;
+      return (int)min(max(v, (int64_t)-1), (int64_t)L + 1);
+    }
   };
   auto finish = [&](int64_t R, double sum) {
     if (R == head_row) {
