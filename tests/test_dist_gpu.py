@@ -180,6 +180,10 @@ def test_step_barrier_times_out_without_peer(pf):
     torch.cuda.synchronize()
     waited = time.time() - t0
     bits = h.device_error()
+    # the barrier-wait diagnostic saw every CTA wait about the 1 s bound
+    wait_ns, ctas = h.dist_wait_ns(reset=True)
+    assert ctas > 0 and 0.5e9 < wait_ns / ctas < 30e9, (wait_ns, ctas)
+    assert h.dist_wait_ns()[0] == 0  # reset
     h.close()
     assert bits & 1, f"expected the wait-timeout bit, got {bits:#x}"
     assert 0.5 < waited < 30

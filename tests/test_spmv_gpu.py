@@ -9,7 +9,7 @@ is an exact integer, so fp64 results must be bit-identical.
 import numpy as np
 import pytest
 
-from csr_cases import CASES, case
+from csr_cases import CASES, case, from_lengths
 
 pytestmark = pytest.mark.gpu
 
@@ -237,3 +237,24 @@ def test_bad_column_index_reported(pf, torch_cuda, handle):
     bits = handle.device_error(clear=True)
     assert bits & 2
     assert handle.device_error() == 0
+
+
+def test_selector_choice(pf, torch_cuda):
+    """The variant query reports what the selector runs: ROWVEC for regular
+    rows (two lanes up to 16 non-zeros per row), NNZROW for power-law rows,
+    for every value size."""
+    torch = torch_cuda
+    rng = np.random.default_rng(51)
+    regular = from_lengths(rng, np.full(20000, 16), 20000)[0]
+    skewed = np.zeros(20001, dtype=np.int64)
+    np.cumsum(np.minimum(np.rint(rng.random(20000) ** (-1 / 1.1)), 5000).astype(np.int64),
+              out=skewed[1:])
+    h = pf.Handle()
+    for rp, want in ((regular, ("rowvec", 2)), (skewed, ("nnzrow", 0))):
+        d_rp = torch.from_numpy(rp.astype(np.int32)).cuda()
+        for vb in (8, 4, 2):
+            assert h.choice(len(rp) - 1, int(rp[-1]), d_rp, vb) == want
+    h.set_variant(2)
+    assert h.choice(len(regular) - 1, int(regular[-1]),
+                    torch.from_numpy(regular).cuda(), 8)[0] == "rowgroup"
+    h.close()
