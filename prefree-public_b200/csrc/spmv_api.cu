@@ -472,11 +472,11 @@ static pf_status launch_nnzsplit_tma(pf_handle h, SpmvParams<VT, IT> prm, cudaSt
 // tile).
 template <typename VT, typename IT>
 static pf_status launch_nnzrow(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st) {
-  // 64 threads, 8 non-zeros per thread, pieces of more than 64 products to
-  // a warp, 16 CTAs per SM: the best of a sweep over 64-256 threads, 4 or 8
-  // non-zeros per thread, 16-64 products per thread piece, 4-32 CTAs per SM
-  // and 1-4 accumulators per piece
-  constexpr int NT = 64, K = 8, LS = 64, MINB = 16;
+  // one-warp CTAs, 8 non-zeros per thread, pieces of more than 64 products
+  // to the warp, 32 CTAs per SM: the best of a sweep over 32-256 threads, 4
+  // or 8 non-zeros per thread, 16-64 products per thread piece, 4-32 CTAs
+  // per SM and 1-4 accumulators per piece
+  constexpr int NT = 32, K = 8, LS = 64, MINB = 32;
   auto kern = spmv_nnzrow_kernel<VT, IT, NT, K, LS, MINB>;
   static int occ_dev[kMaxDevices] = {};
   int &occ = occ_dev[h->device % kMaxDevices];

@@ -1,6 +1,7 @@
 // NNZROW variant: equal-nnz CTA slices walked in tiles of NT * K non-zeros;
 // products parked in shared memory, each row's piece of a tile summed by one
-// thread (short pieces) or one warp (long pieces).
+// thread (short pieces) or one warp (long pieces). Shipped with one-warp CTAs
+// (NT = 32), whose barriers are warp primitives.
 //
 // Slice c holds the non-zeros [S0, S1) = [base + c*T, min(base + (c+1)*T,
 // base + nnz)) (slice geometry and the ownership of cut and empty rows as in
@@ -58,6 +59,21 @@ spmv_nnzrow_kernel(const SpmvParams<VT, IT> P) {
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
+  // a one-warp CTA synchronises with warp primitives (shared memory is
+  // ordered among the warp's lanes by __syncwarp)
+  auto cta_sync = [&]() {
+    if constexpr (NT == 32) __syncwarp();
+    else __syncthreads();
+  };
+  auto cta_count = [&](bool pred) -> int {
+    if constexpr (NT == 32) {
+      const int c = __popc(__ballot_sync(0xffffffffu, pred));
+      __syncwarp();
+      return c;
+    } else {
+      return __syncthreads_count(pred);
+    }
+  };
   const int64_t c = blockIdx.x;
   const int64_t base = (int64_t)__ldg(P.row_ptr);
   // nnz must equal row_ptr[m] - row_ptr[0], or slices would read outside
@@ -98,7 +114,7 @@ spmv_nnzrow_kernel(const SpmvParams<VT, IT> P) {
     s_nlong[tid] = 0;
     s_carry[tid] = 0.0;
   }
-  __syncthreads();
+  cta_sync();
   if (s_meta[1] != 0 && s_meta[0] == 0) {
     // row_ptr[0] > S0 is impossible for a non-decreasing row_ptr
     if (tid == 0) atomicOr(P.err, PF_DEVERR_ROWPTR);
@@ -156,7 +172,7 @@ spmv_nnzrow_kernel(const SpmvParams<VT, IT> P) {
       for (int k = 0; k < K; ++k) prod[tid + k * NT] = (double)vn[k] * (double)xv[k];
     }
     if (i + 1 < ntiles) load_tile(tb + TILE);
-    __syncthreads();
+    cta_sync();
     // the next tile's list and carry: every thread has read the previous
     // tile's carry from that copy before the barrier above
     if (tid == 0) {
@@ -184,7 +200,7 @@ spmv_nnzrow_kernel(const SpmvParams<VT, IT> P) {
           else s_carry[par] = sum;
         }
       }
-      const int nf = __syncthreads_count(fin);
+      const int nf = cta_count(fin);
       done += nf;
       if (nf < NT) break;
       // every row of the window ends in this tile: the next window
@@ -208,7 +224,7 @@ spmv_nnzrow_kernel(const SpmvParams<VT, IT> P) {
         else s_carry[par] = sum;
       }
     }
-    __syncthreads();  // the next carry is in place; the products may be rewritten
+    cta_sync();  // the next carry is in place; the products may be rewritten
     carry = s_carry[par];
     r_cur += done;
   }
