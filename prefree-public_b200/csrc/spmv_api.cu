@@ -486,8 +486,12 @@ static pf_status launch_nnzrow(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t
     occ = std::max(1, o);
   }
   const int64_t ctas = (int64_t)h->num_sms * occ;
-  const int64_t T = h->slice_override > 0 ? h->slice_override
-                                          : std::max<int64_t>(ceil_div(prm.nnz, ctas), (int64_t)NT * K);
+  // slices of whole 32-element runs: with row_ptr[0] = 0 every warp load of
+  // 32 column or value elements then covers whole 32-byte sectors (4 and 8
+  // of them) instead of straddling one more
+  const int64_t T = h->slice_override > 0
+                        ? h->slice_override
+                        : std::max<int64_t>(ceil_div(ceil_div(prm.nnz, ctas), 32) * 32, (int64_t)NT * K);
   const int64_t P = ceil_div(prm.nnz, T);
   PF_CHECK_ARG(P <= INT32_MAX, "too many slices");
   PF_CHECK_ARG(T < INT32_MAX, "slice too long");
