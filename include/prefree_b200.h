@@ -65,8 +65,8 @@ uint64_t pf_launch_count(void);
 pf_status pf_handle_create(pf_handle *out);
 pf_status pf_handle_destroy(pf_handle h);
 pf_status pf_handle_set_variant(pf_handle h, int variant);
-/* Testing knob: fixed non-zeros per CTA slice for NNZSPLIT (0 = automatic).
- * Small slices force many rows to be cut between CTAs. */
+/* Testing knob: fixed non-zeros per CTA slice for NNZSPLIT and NNZROW
+ * (0 = automatic). Small slices force many rows to be cut between CTAs. */
 pf_status pf_handle_set_slice(pf_handle h, int64_t slice_nnz);
 /* Synchronizes the device, returns the device error bits, optionally clears. */
 pf_status pf_handle_device_error(pf_handle h, uint32_t *bits, int clear);
