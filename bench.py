@@ -535,15 +535,18 @@ def main():
     ev_pairs.clear()
 
     # ---- timed region ------------------------------------------------------------
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
     if args.path == "fused":
         h.dist_wait_ns(reset=True)
     launches0 = pf.launch_count()
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
+    # the clock sampler starts (NVML initialisation, milliseconds that differ
+    # from rank to rank) before the barrier, so that every rank records its
+    # start event right after leaving the same barrier
     with ClockSampler(local) as clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         t_start.record(stream)
         for _ in range(args.steps):
             st = it.step()
