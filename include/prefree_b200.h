@@ -216,9 +216,13 @@ pf_status pf_spmv_noalloc_f64_i32(int64_t m, int64_t n, int64_t nnz,
 
 /* ---- host-buffer call (one multiply, copies in and out) ---------------------
  * Same arithmetic as pf_spmv_*, on HOST arrays: copies row_ptr/col/val/x in
- * (and y when beta != 0), multiplies once, copies y out, synchronizes. Device
- * buffers are cached in the handle and reused across calls. Pinned host memory
- * gives full PCIe bandwidth; pageable memory works too.                       */
+ * (and y when beta != 0), multiplies once, copies y out, synchronizes. col/val
+ * travel in row chunks of about equal nnz (256 MB each, at most 16; the
+ * environment variable PF_HOST_CHUNK_BYTES overrides the size) on a copy
+ * stream of the handle, and each chunk is multiplied and its rows of y copied
+ * out on `stream` while the next chunks are copied in. Device buffers are
+ * cached in the handle and reused across calls. Pinned host memory gives full
+ * PCIe bandwidth and the overlap; pageable memory works too.                 */
 pf_status pf_spmv_host_f64_i32(pf_handle h, int64_t m, int64_t n, int64_t nnz,
                                const int32_t *row_ptr, const int32_t *col_idx,
                                const double *val, double alpha,

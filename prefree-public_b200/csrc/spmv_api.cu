@@ -101,9 +101,12 @@ struct pf_handle_s {
   unsigned long long *dist_wait = nullptr;  // step-barrier wait, ns summed over CTAs
   int64_t dist_grid = 0;                    // CTAs of the last fused launch
   int64_t dist_cap = 0;
-  // host-call buffers
+  // host-call buffers, and the copy stream and events of the pipelined
+  // host call (created on first use)
   void *hbuf[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
   size_t hcap[5] = {0, 0, 0, 0, 0};
+  cudaStream_t hcopy = nullptr;
+  cudaEvent_t hev[17] = {};
 };
 
 namespace pf {
@@ -358,7 +361,8 @@ template <typename VT, typename IT>
 static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
                              const IT *row_ptr, const int32_t *col,
                              const VT *val, double alpha, const VT *x,
-                             double beta, VT *y, cudaStream_t st) {
+                             double beta, VT *y, cudaStream_t st,
+                             const pf_variant_choice *chosen = nullptr) {
   PF_CHECK_ARG(h != nullptr, "null handle");
   PF_CHECK_ARG(m >= 0 && n >= 0 && nnz >= 0, "negative size (m=%lld n=%lld nnz=%lld)",
                (long long)m, (long long)n, (long long)nnz);
@@ -388,8 +392,12 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
   }
 
   pf_variant_choice ch;
-  pf_status s = select_variant<IT>(h, m, nnz, row_ptr, st, &ch);
-  if (s != PF_OK) return s;
+  if (chosen) {
+    ch = *chosen;
+  } else {
+    pf_status s = select_variant<IT>(h, m, nnz, row_ptr, st, &ch);
+    if (s != PF_OK) return s;
+  }
   ch = for_values(h, ch, (int)sizeof(VT));
 
   SpmvParams<VT, IT> prm;
@@ -626,7 +634,43 @@ static pf_status launch_spmm(pf_handle h, int64_t m, int64_t n, int64_t nnz, con
   return PF_OK;
 }
 
-// Host-buffer call: copy in, one multiply, copy out.
+// The selector's choice for a matrix whose row_ptr is in host memory: the
+// same evenly spaced sample of row lengths as sample_lengths_kernel.
+template <typename IT>
+static pf_variant_choice choose_host(pf_handle h, int64_t m, int64_t nnz, const IT *row_ptr) {
+  if (h->variant != PF_VARIANT_AUTO) {
+    const double avg = m > 0 ? (double)nnz / (double)m : 0.0;
+    return pf_variant_choice{h->variant, h->variant == PF_VARIANT_ROWVEC ? rowvec_lanes(avg)
+                                                                         : rowgroup_lanes(avg)};
+  }
+  const int S = (int)std::min<int64_t>(m, kSampleRows);
+  int64_t sample[kSampleRows];
+  for (int i = 0; i < S; ++i) {
+    const int64_t r = (int64_t)((__int128)m * (2 * i + 1) / (2 * S));
+    sample[i] = (int64_t)row_ptr[r + 1] - (int64_t)row_ptr[r];
+  }
+  return choose_from_stats(m, nnz, sample, S);
+}
+
+// Host-buffer call. x, row_ptr (and y when beta != 0) are copied first, then
+// col/val in row chunks of about equal nnz, all on the handle's copy stream;
+// chunk i's multiply and the copy-out of its rows of y run on the caller's
+// stream as soon as chunk i has arrived, so the multiplies and the copy-out
+// overlap the copy-in of the chunks after it. Returns when y is in place.
+constexpr size_t kHostChunkBytes = size_t(256) << 20;
+constexpr int kHostMaxChunks = 16;
+
+// col/val bytes per chunk: 256 MB, or PF_HOST_CHUNK_BYTES (tests use small
+// chunks to run the pipeline on small matrices)
+static size_t host_chunk_bytes() {
+  const char *e = std::getenv("PF_HOST_CHUNK_BYTES");
+  if (e && *e) {
+    const long long v = std::atoll(e);
+    if (v > 0) return (size_t)v;
+  }
+  return kHostChunkBytes;
+}
+
 template <typename VT, typename IT>
 static pf_status host_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
                            const IT *row_ptr, const int32_t *col, const VT *val,
@@ -639,6 +683,10 @@ static pf_status host_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
   PF_CHECK_ARG(nnz == 0 || (col && val && x), "null col/val/x with nnz > 0");
   const int64_t base = (int64_t)row_ptr[0];
   PF_CHECK_ARG((int64_t)row_ptr[m] - base == nnz, "nnz != row_ptr[m] - row_ptr[0]");
+  int cur = 0;
+  PF_CUDA_TRY(cudaGetDevice(&cur));
+  PF_CHECK_ARG(cur == h->device, "handle bound to device %d, current device is %d", h->device,
+               cur);
   const size_t need[5] = {sizeof(IT) * (size_t)(m + 1), sizeof(int32_t) * (size_t)nnz,
                           sizeof(VT) * (size_t)nnz, sizeof(VT) * (size_t)n,
                           sizeof(VT) * (size_t)m};
@@ -651,26 +699,83 @@ static pf_status host_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
       h->hcap[i] = std::max<size_t>(need[i], 256);
     }
   }
+  if (!h->hcopy) {
+    PF_CUDA_TRY(cudaStreamCreateWithFlags(&h->hcopy, cudaStreamNonBlocking));
+    for (int i = 0; i <= kHostMaxChunks; ++i)
+      PF_CUDA_TRY(cudaEventCreateWithFlags(&h->hev[i], cudaEventDisableTiming));
+  }
   IT *d_rp = (IT *)h->hbuf[0];
   int32_t *d_col = (int32_t *)h->hbuf[1];
   VT *d_val = (VT *)h->hbuf[2];
   VT *d_x = (VT *)h->hbuf[3];
   VT *d_y = (VT *)h->hbuf[4];
-  PF_CUDA_TRY(cudaMemcpyAsync(d_rp, row_ptr, need[0], cudaMemcpyHostToDevice, st));
-  if (nnz > 0) {
-    PF_CUDA_TRY(cudaMemcpyAsync(d_col, col + base, need[1], cudaMemcpyHostToDevice, st));
-    PF_CUDA_TRY(cudaMemcpyAsync(d_val, val + base, need[2], cudaMemcpyHostToDevice, st));
+  const cudaStream_t cs = h->hcopy;
+
+  // chunk boundaries: rows [r[i], r[i+1]) starting at the first row whose
+  // start reaches i/C of the non-zeros
+  const size_t mat_bytes = need[1] + need[2];
+  const int C = (int)std::max<size_t>(1, std::min<size_t>(kHostMaxChunks, mat_bytes / host_chunk_bytes()));
+  int64_t r[kHostMaxChunks + 1];
+  r[0] = 0;
+  for (int i = 1; i < C; ++i) {
+    const int64_t target = base + (int64_t)((__int128)nnz * i / C);
+    int64_t lo = r[i - 1], hi = m;  // first row with row_ptr[row] >= target
+    while (lo < hi) {
+      const int64_t mid = lo + (hi - lo) / 2;
+      if ((int64_t)row_ptr[mid] < target) lo = mid + 1;
+      else hi = mid;
+    }
+    r[i] = lo;
   }
-  if (n > 0) PF_CUDA_TRY(cudaMemcpyAsync(d_x, x, need[3], cudaMemcpyHostToDevice, st));
-  if (beta != 0.0) PF_CUDA_TRY(cudaMemcpyAsync(d_y, y, need[4], cudaMemcpyHostToDevice, st));
+  r[C] = m;
+  const pf_variant_choice ch = choose_host<IT>(h, m, nnz, row_ptr);
+
+  // the copy stream starts after the caller's earlier work on st
+  PF_CUDA_TRY(cudaEventRecord(h->hev[kHostMaxChunks], st));
+  PF_CUDA_TRY(cudaStreamWaitEvent(cs, h->hev[kHostMaxChunks], 0));
+  pf_status status = PF_OK;
+  auto fail = [&](cudaError_t e, const char *what) {
+    if (e != cudaSuccess && status == PF_OK) {
+      set_error("%s: %s", what, cudaGetErrorString(e));
+      status = PF_ERR_CUDA;
+    }
+  };
+  fail(cudaMemcpyAsync(d_rp, row_ptr, need[0], cudaMemcpyHostToDevice, cs), "copy row_ptr");
+  if (n > 0 && nnz > 0) fail(cudaMemcpyAsync(d_x, x, need[3], cudaMemcpyHostToDevice, cs), "copy x");
+  if (beta != 0.0) fail(cudaMemcpyAsync(d_y, y, need[4], cudaMemcpyHostToDevice, cs), "copy y");
+  for (int i = 0; i < C && status == PF_OK; ++i) {
+    const int64_t e0 = (int64_t)row_ptr[r[i]] - base, e1 = (int64_t)row_ptr[r[i + 1]] - base;
+    if (e1 > e0) {
+      fail(cudaMemcpyAsync(d_col + e0, col + base + e0, sizeof(int32_t) * (size_t)(e1 - e0),
+                           cudaMemcpyHostToDevice, cs), "copy col");
+      fail(cudaMemcpyAsync(d_val + e0, val + base + e0, sizeof(VT) * (size_t)(e1 - e0),
+                           cudaMemcpyHostToDevice, cs), "copy val");
+    }
+    fail(cudaEventRecord(h->hev[i], cs), "record chunk event");
+  }
   // Device arrays hold the slice only: shift so absolute row_ptr values land
-  // at element 0 (the kernel only touches [base, base + nnz)).
-  pf_status s = launch_spmv<VT, IT>(h, m, n, nnz, d_rp, d_col - base, d_val - base,
-                                    alpha, d_x, beta, d_y, st);
-  if (s != PF_OK) return s;
-  PF_CUDA_TRY(cudaMemcpyAsync(y, d_y, need[4], cudaMemcpyDeviceToHost, st));
-  PF_CUDA_TRY(cudaStreamSynchronize(st));
-  return PF_OK;
+  // at element 0 (a chunk's kernel only touches its own [row_ptr[r], row_ptr[r_end])).
+  for (int i = 0; i < C && status == PF_OK; ++i) {
+    const int64_t mi = r[i + 1] - r[i];
+    if (mi == 0) continue;
+    const int64_t nz = (int64_t)row_ptr[r[i + 1]] - (int64_t)row_ptr[r[i]];
+    fail(cudaStreamWaitEvent(st, h->hev[i], 0), "wait for chunk");
+    if (status != PF_OK) break;
+    pf_status s = launch_spmv<VT, IT>(h, mi, n, nz, d_rp + r[i], d_col - base, d_val - base,
+                                      alpha, d_x, beta, d_y + r[i], st, &ch);
+    if (s != PF_OK) {
+      status = s;
+      break;
+    }
+    fail(cudaMemcpyAsync(y + r[i], d_y + r[i], sizeof(VT) * (size_t)mi, cudaMemcpyDeviceToHost, st),
+         "copy y out");
+  }
+  // both streams drain before the buffers can be reused or y read
+  const cudaError_t e1 = cudaStreamSynchronize(cs);
+  const cudaError_t e2 = cudaStreamSynchronize(st);
+  fail(e1, "copy stream");
+  fail(e2, "stream");
+  return status;
 }
 
 }  // namespace pf
@@ -715,6 +820,11 @@ pf_status pf_handle_destroy(pf_handle h) {
   if (h->err) cudaFree(h->err);
   for (int i = 0; i < 5; ++i)
     if (h->hbuf[i]) cudaFree(h->hbuf[i]);
+  if (h->hcopy) {
+    cudaStreamDestroy(h->hcopy);
+    for (int i = 0; i <= kHostMaxChunks; ++i)
+      if (h->hev[i]) cudaEventDestroy(h->hev[i]);
+  }
   if (h->dist_part) cudaFree(h->dist_part);
   if (h->sample_dev) cudaFree(h->sample_dev);
   if (h->sample_host) cudaFreeHost(h->sample_host);

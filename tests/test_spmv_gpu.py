@@ -201,6 +201,37 @@ def test_host_buffer_call(pf, oracle, torch_cuda, handle):
     assert ok, worst
 
 
+@pytest.mark.parametrize("name", ["mixed_long", "powerlaw", "empty_edges", "row0_long",
+                                  "empty_matrix"])
+@pytest.mark.parametrize("vdt", [np.float64, np.float32])
+@pytest.mark.parametrize("idt", [np.int32, np.int64])
+def test_host_buffer_pipelined_chunks(pf, oracle, torch_cuda, handle, monkeypatch, name, vdt, idt):
+    """The host-buffer call copies col/val in row chunks of about equal nnz and
+    multiplies each chunk as it arrives. 4 KB chunks (16 at most) put chunk
+    boundaries among empty and long rows; beta != 0, and a row slice of the
+    host CSR whose first offset is not 0."""
+    monkeypatch.setenv("PF_HOST_CHUNK_BYTES", "4096")
+    rp, col, val, n = case(name, seed=31)
+    rp = rp.astype(idt)
+    rng = np.random.default_rng(32)
+    x = rng.uniform(-1, 1, n).astype(vdt)
+    val = val.astype(vdt)
+    m = len(rp) - 1
+    y0 = rng.uniform(-1, 1, m).astype(vdt)
+    y = y0.copy()
+    pf.spmv_host(handle, rp, col, val, x, y, alpha=0.75, beta=-0.5)
+    check(oracle, y.astype(np.float64), rp, col, val, x, vdt, alpha=0.75, beta=-0.5, y0=y0)
+    if m > 10:
+        r0, r1 = m // 7, m - m // 5
+        ys = np.zeros(r1 - r0, dtype=vdt)
+        pf.spmv_host(handle, rp[r0:r1 + 1], col, val, x, ys, m=r1 - r0, n=n)
+        full = oracle.serial(rp, col, val, x)
+        a, _ = oracle.abs_comp(rp, col, val, x)
+        ok, worst, _ = oracle.tolerance_report(ys.astype(np.float64), full[r0:r1], a[r0:r1],
+                                               EPS[vdt])
+        assert ok, worst
+
+
 def test_prefree_entry_point(pf, oracle, torch_cuda, monkeypatch):
     """The reference's call shape: host arrays, int32 offsets, Y overwritten,
     timing outputs in ms (include/PreFree.h:3-5, preFreeSpMV.cu:563-662)."""
