@@ -478,13 +478,13 @@ static pf_status launch_nnzsplit_tma(pf_handle h, SpmvParams<VT, IT> prm, cudaSt
 
 // NNZROW: one wave of resident CTAs, one equal-nnz slice each (at least one
 // tile).
-template <typename VT, typename IT>
-static pf_status launch_nnzrow(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st) {
-  // one-warp CTAs, 8 non-zeros per thread, pieces of more than 64 products
-  // to the warp, 32 CTAs per SM: the best of a sweep over 32-256 threads, 4
-  // or 8 non-zeros per thread, 16-64 products per thread piece, 4-32 CTAs
+template <typename VT, typename IT, int KK>
+static pf_status launch_nnzrow_k(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st) {
+  // one-warp CTAs, KK non-zeros per thread, pieces of more than 64 products
+  // to the warp, 32 CTAs per SM: the best of a sweep over 32-256 threads,
+  // 4-16 non-zeros per thread, 16-128 products per thread piece, 4-32 CTAs
   // per SM and 1-4 accumulators per piece
-  constexpr int NT = 32, K = 8, LS = 64, MINB = 32;
+  constexpr int NT = 32, K = KK, LS = 64, MINB = 32;
   auto kern = spmv_nnzrow_kernel<VT, IT, NT, K, LS, MINB>;
   static int occ_dev[kMaxDevices] = {};
   int &occ = occ_dev[h->device % kMaxDevices];
@@ -514,6 +514,15 @@ static pf_status launch_nnzrow(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t
   count_launch();
   PF_CUDA_TRY(cudaGetLastError());
   return PF_OK;
+}
+
+// 8 non-zeros per thread for 8-byte values, 10 for 4- and 2-byte values,
+// whose next-tile elements take fewer registers (config 3 fp32 163.7 ->
+// 159.9 us, fp16 168.4 -> 162.5; 12 and 16 non-zeros were slower)
+template <typename VT, typename IT>
+static pf_status launch_nnzrow(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st) {
+  if constexpr (sizeof(VT) <= 4) return launch_nnzrow_k<VT, IT, 10>(h, prm, st);
+  else return launch_nnzrow_k<VT, IT, 8>(h, prm, st);
 }
 
 // The one-time work of the first multiply with a matrix: the variant choice

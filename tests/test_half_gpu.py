@@ -75,3 +75,23 @@ def test_half_alpha_beta_int64(pf, oracle, fmt, idt):
     y, v64, x64 = run_half(pf, torch, h, rp, col, val, x, n, tdt, idt, alpha=0.75, beta=-1.25, y0=y0)
     h.close()
     check(oracle, y, rp, col, v64, x64, p, tmin, alpha=0.75, beta=-1.25, y0=y0)
+
+
+@pytest.mark.parametrize("fmt", ["f16", "bf16"])
+@pytest.mark.parametrize("name", ["powerlaw", "mixed_long", "row0_long", "empty_edges"])
+@pytest.mark.parametrize("slice_nnz", [1, 63, 319, 320, 640, 1000])
+def test_half_nnzrow_cut_rows(pf, oracle, fmt, name, slice_nnz):
+    """NNZROW walks 320-element tiles with 16-bit values: slices shorter and
+    longer than a tile, ending on and off tile boundaries, cut every kind of
+    row."""
+    import torch
+    tdt = torch.float16 if fmt == "f16" else torch.bfloat16
+    p, tmin = (10, 2.0 ** -24) if fmt == "f16" else (7, 0.0)
+    rp, col, val, n = case(name, seed=65)
+    x = np.random.default_rng(66).uniform(-1, 1, n)
+    h = pf.Handle()
+    h.set_variant(VARIANTS["nnzrow"])
+    h.set_slice(slice_nnz)
+    y, v64, x64 = run_half(pf, torch, h, rp, col, val, x, n, tdt, np.int64)
+    h.close()
+    check(oracle, y, rp, col, v64, x64, p, tmin)
