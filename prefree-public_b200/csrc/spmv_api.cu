@@ -516,13 +516,14 @@ static pf_status launch_nnzrow_k(pf_handle h, SpmvParams<VT, IT> prm, cudaStream
   return PF_OK;
 }
 
-// 8 non-zeros per thread for 8-byte values, 10 for 4- and 2-byte values,
-// whose next-tile elements take fewer registers (config 3 fp32 163.7 ->
-// 159.9 us, fp16 168.4 -> 162.5; 12 and 16 non-zeros were slower)
+// 7 non-zeros per thread for 8-byte values, 10 for 4- and 2-byte values,
+// whose next-tile elements take fewer registers (config 3, us: fp64 K = 6
+// 180.1, 7 176.1, 8 178.0, 9 182.0; fp32 K = 8 163.7, 10 159.9; fp16 K = 8
+// 168.4, 10 162.5; 12 and 16 non-zeros were slower)
 template <typename VT, typename IT>
 static pf_status launch_nnzrow(pf_handle h, SpmvParams<VT, IT> prm, cudaStream_t st) {
   if constexpr (sizeof(VT) <= 4) return launch_nnzrow_k<VT, IT, 10>(h, prm, st);
-  else return launch_nnzrow_k<VT, IT, 8>(h, prm, st);
+  else return launch_nnzrow_k<VT, IT, 7>(h, prm, st);
 }
 
 // The one-time work of the first multiply with a matrix: the variant choice

@@ -1,7 +1,7 @@
 // NNZROW variant: equal-nnz CTA slices walked in tiles of NT * K non-zeros;
 // products parked in shared memory, each row's piece of a tile summed by one
 // thread (short pieces) or one warp (long pieces). Shipped with one-warp CTAs
-// (NT = 32), whose barriers are warp primitives, and K = 8 non-zeros per
+// (NT = 32), whose barriers are warp primitives, and K = 7 non-zeros per
 // thread for 8-byte values, 10 for 4- and 2-byte values.
 //
 // Slice c holds the non-zeros [S0, S1) = [base + c*T, min(base + (c+1)*T,

@@ -1,11 +1,11 @@
 """NNZROW at the edges of its tile walk, against the CPU oracle.
 
-A tile is 256 non-zeros of a slice with fp64 values (8 per thread of a
+A tile is 224 non-zeros of a slice with fp64 values (7 per thread of a
 one-warp CTA) and 320 with fp32 or 16-bit values (10 per thread); its rows
 are taken in windows of 32 (one per thread), a row piece of more than 64
 products goes to a warp, and the sum of the row left open at the tile's end
 is carried to the next tile. These matrices put that walk at its edges: long
-runs of one-non-zero rows (a tile of row ends: eight or ten windows), short
+runs of one-non-zero rows (a tile of row ends: seven or ten windows), short
 rows mixed with empty ones,
 heavy tails (long pieces next to short ones), and slice lengths around and
 at multiples of the tile, so that a slice's cut first row ends inside a tile
@@ -93,7 +93,7 @@ def check(oracle, y, rp, col, val, x, vdt, alpha=1.0, beta=0.0, y0=None):
 
 
 @pytest.mark.parametrize("name", NAMES)
-@pytest.mark.parametrize("slice_nnz", [0, 1, 63, 256, 319, 320, 511, 512, 640, 768, 1000, 4096])
+@pytest.mark.parametrize("slice_nnz", [0, 1, 63, 223, 224, 256, 319, 320, 448, 511, 512, 640, 768, 1000, 4096])
 @pytest.mark.parametrize("idt", [np.int32, np.int64])
 @pytest.mark.parametrize("vdt", [np.float64, np.float32])
 def test_tile_walk_slices(pf, oracle, torch_cuda, ws_handle, name, slice_nnz, idt, vdt):
