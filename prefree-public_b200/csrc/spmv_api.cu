@@ -264,6 +264,25 @@ static pf_status launch_rowgroup(pf_handle h, const SpmvParams<VT, IT> &prm, cud
   return PF_OK;
 }
 
+// ROWVEC for long rows: 16 lanes per row, one row per lane group, and each
+// lane's next block loaded before the current block's gathers (two blocks of
+// the row in flight per lane), 4 CTAs per SM. Config 4 (2000 per row):
+// 207.8-208.2 us against 215.1-215.9 for two rows per group without the
+// early loads; 32 lanes per row, two rows per group with early loads (3
+// CTAs per SM, spills) and 3-8 CTAs per SM were slower.
+template <typename VT, typename IT>
+static pf_status launch_rowvec_long(pf_handle h, const SpmvParams<VT, IT> &prm, cudaStream_t st) {
+  constexpr int V = 16, U = 1, NTB = 256, MINB = 4;
+  const int64_t rows_per_block = (int64_t)(NTB / 32) * (32 / V) * U;
+  const int64_t want = ceil_div(prm.m, rows_per_block);
+  const int64_t cap = (int64_t)h->num_sms * 16;
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min(want, cap));
+  spmv_rowvec_kernel<VT, IT, V, U, NTB, MINB, false, true><<<grid, NTB, 0, st>>>(prm);
+  count_launch();
+  PF_CUDA_TRY(cudaGetLastError());
+  return PF_OK;
+}
+
 template <typename VT, typename IT, int V>
 static pf_status launch_rowvec(pf_handle h, const SpmvParams<VT, IT> &prm, cudaStream_t st) {
   // U = 2 rows per lane group in flight, built for 4 CTAs per SM (64
@@ -438,7 +457,11 @@ static pf_status launch_spmv(pf_handle h, int64_t m, int64_t n, int64_t nnz,
       case 2: return launch_rowvec<VT, IT, 2>(h, prm, st);
       case 4: return launch_rowvec<VT, IT, 4>(h, prm, st);
       case 8: return launch_rowvec<VT, IT, 8>(h, prm, st);
-      case 16: return launch_rowvec<VT, IT, 16>(h, prm, st);
+      case 16:
+        // long rows (every lane walks two blocks or more): one row per lane
+        // group with the next block's loads issued ahead
+        if (prm.nnz >= 128 * prm.m) return launch_rowvec_long<VT, IT>(h, prm, st);
+        return launch_rowvec<VT, IT, 16>(h, prm, st);
       default: return launch_rowvec<VT, IT, 32>(h, prm, st);
     }
   }

@@ -11,6 +11,9 @@
 // 16-byte block that contains a valid element. Requires col and val to start
 // on 16-byte boundaries (the host falls back to ROWGROUP otherwise).
 //
+// PIPE (long rows): a lane loads its next block of each row before it
+// gathers and sums the current one, so two blocks per row are in flight.
+//
 // Selected for regular rows (uniform 16/row, the Laplacian, banded 32/row,
 // 2000/row). Correct for any CSR; an unusually long row only slows its group.
 #pragma once
@@ -118,7 +121,8 @@ __device__ __forceinline__ void dist_norm_epilogue(const DistOut &D, double nsq)
   __threadfence_system();
 }
 
-template <typename VT, typename IT, int V, int U, int NTB, int MINB = 1, bool DIST = false>
+template <typename VT, typename IT, int V, int U, int NTB, int MINB = 1, bool DIST = false,
+          bool PIPE = false>
 __global__ void __launch_bounds__(NTB, MINB)
 spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const DistOut D = DistOut{}) {
   constexpr int GPW = 32 / V;  // row groups per warp
@@ -224,37 +228,85 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const DistOut D = DistOut{}) {
       }
       o[u] = 4 * lig;
     }
-    bool more = true;
-    while (more) {
+    // a lane's block at offset oo of row u: the column block and the value
+    // halves that hold an element of the row
+    auto load_blk = [&](int u, int oo, int4 &cb, VT (&vb)[4]) {
+      const bool act = oo < len[u];
+      const int64_t q = q0[u] + oo;
+      cb = act ? __ldcs(reinterpret_cast<const int4 *>(P.col + q)) : make_int4(0, 0, 0, 0);
+      Block4<VT>::load(P.val, q, act && oo + 1 >= lo[u], act && oo + 2 < len[u], vb);
+    };
+    if constexpr (PIPE) {
+      // the next block's loads are issued before this block's gathers, so a
+      // lane keeps two blocks of every row in flight
       int4 c4[U];
       VT v4[U][4];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const bool act = o[u] < len[u];
-        const int64_t q = q0[u] + o[u];
-        c4[u] = act ? __ldcs(reinterpret_cast<const int4 *>(P.col + q)) : make_int4(0, 0, 0, 0);
-        Block4<VT>::load(P.val, q, act && o[u] + 1 >= lo[u], act && o[u] + 2 < len[u], v4[u]);
-      }
-      VT xv[U][4];
+      for (int u = 0; u < U; ++u) load_blk(u, o[u], c4[u], v4[u]);
+      bool more = true;
+      while (more) {
+        int4 c4n[U];
+        VT v4n[U][4];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int cc[4] = {c4[u].x, c4[u].y, c4[u].z, c4[u].w};
+        for (int u = 0; u < U; ++u) load_blk(u, o[u] + 4 * V, c4n[u], v4n[u]);
+        VT xv[U][4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int el = o[u] + i;
-          const bool use = el >= lo[u] && el < len[u];
-          const bool inb = (uint32_t)cc[i] < n;
-          bad |= use && !inb;
-          xv[u][i] = (use && inb) ? ptx::ldg_x(P.x + cc[i]) : VT(0);
+        for (int u = 0; u < U; ++u) {
+          const int cc[4] = {c4[u].x, c4[u].y, c4[u].z, c4[u].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int el = o[u] + i;
+            const bool use = el >= lo[u] && el < len[u];
+            const bool inb = (uint32_t)cc[i] < n;
+            bad |= use && !inb;
+            xv[u][i] = (use && inb) ? ptx::ldg_x(P.x + cc[i]) : VT(0);
+          }
+        }
+        more = false;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[u] += (double)v4[u][i] * (double)xv[u][i];
+          o[u] += 4 * V;
+          more |= o[u] < len[u];
+          c4[u] = c4n[u];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) v4[u][i] = v4n[u][i];
         }
       }
-      more = false;
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[u] += (double)v4[u][i] * (double)xv[u][i];
-        o[u] += 4 * V;
-        more |= o[u] < len[u];
+    } else {
+      bool more = true;
+      while (more) {
+        int4 c4[U];
+        VT v4[U][4];
+  #pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const bool act = o[u] < len[u];
+          const int64_t q = q0[u] + o[u];
+          c4[u] = act ? __ldcs(reinterpret_cast<const int4 *>(P.col + q)) : make_int4(0, 0, 0, 0);
+          Block4<VT>::load(P.val, q, act && o[u] + 1 >= lo[u], act && o[u] + 2 < len[u], v4[u]);
+        }
+        VT xv[U][4];
+  #pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int cc[4] = {c4[u].x, c4[u].y, c4[u].z, c4[u].w};
+  #pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int el = o[u] + i;
+            const bool use = el >= lo[u] && el < len[u];
+            const bool inb = (uint32_t)cc[i] < n;
+            bad |= use && !inb;
+            xv[u][i] = (use && inb) ? ptx::ldg_x(P.x + cc[i]) : VT(0);
+          }
+        }
+        more = false;
+  #pragma unroll
+        for (int u = 0; u < U; ++u) {
+  #pragma unroll
+          for (int i = 0; i < 4; ++i) acc[u] += (double)v4[u][i] * (double)xv[u][i];
+          o[u] += 4 * V;
+          more |= o[u] < len[u];
+        }
       }
     }
     if (bad) atomicOr(P.err, PF_DEVERR_BOUNDS);

@@ -57,6 +57,12 @@ def case(name, seed=0):
         lens = rng.integers(0, 6, size=8000)
         lens[[5, 700, 701, 4000, 7999]] = [9000, 4000, 12000, 2500, 7000]
         return (*from_lengths(rng, lens, 8000), 8000)
+    if name == "long_rows":
+        # rows of 128-600 non-zeros (the long-row ROWVEC path: every lane
+        # walks two blocks or more), with empty, 1-7 and one 20000-long row
+        lens = rng.integers(128, 600, size=2000)
+        lens[[0, 3, 500, 501, 1200, 1999]] = [0, 1, 3, 7, 20000, 0]
+        return (*from_lengths(rng, lens, 30000), 30000)
     if name == "unsorted":
         lens = rng.integers(0, 30, size=3000)
         return (*from_lengths(rng, lens, 2000, sorted_cols=False), 2000)
@@ -64,7 +70,7 @@ def case(name, seed=0):
 
 
 CASES = ["tiny", "empty_matrix", "one_long_row", "row0_long", "empty_edges", "powerlaw",
-         "uniform16", "mixed_long", "unsorted"]
+         "uniform16", "mixed_long", "unsorted", "long_rows"]
 
 
 def gen_config_host(pf, spec, threads=None):

@@ -47,7 +47,7 @@ def check(oracle, y, rp, col, v64, x64, p, tmin, alpha=1.0, beta=0.0, y0=None):
 @pytest.mark.parametrize("fmt", ["f16", "bf16"])
 @pytest.mark.parametrize("variant", list(VARIANTS))
 @pytest.mark.parametrize("name", ["tiny", "powerlaw", "mixed_long", "row0_long", "empty_edges",
-                                  "uniform16"])
+                                  "uniform16", "long_rows"])
 def test_half_cases_variants(pf, oracle, fmt, variant, name):
     import torch
     tdt = torch.float16 if fmt == "f16" else torch.bfloat16

@@ -134,8 +134,9 @@ def test_unaligned_array_starts(pf, oracle, torch_cuda, variant_handle, offset):
 
 @pytest.mark.parametrize("alpha,beta", [(2.5, 0.0), (1.0, 1.0), (-0.75, 0.5), (0.0, 2.0)])
 @pytest.mark.parametrize("vdt", [np.float64, np.float32])
-def test_alpha_beta(pf, oracle, torch_cuda, handle, alpha, beta, vdt):
-    rp, col, val, n = case("mixed_long", seed=5)
+@pytest.mark.parametrize("name", ["mixed_long", "long_rows"])
+def test_alpha_beta(pf, oracle, torch_cuda, handle, alpha, beta, vdt, name):
+    rp, col, val, n = case(name, seed=5)
     rng = np.random.default_rng(6)
     x = rng.uniform(-1, 1, n)
     y0 = rng.uniform(-1, 1, len(rp) - 1)
@@ -143,7 +144,7 @@ def test_alpha_beta(pf, oracle, torch_cuda, handle, alpha, beta, vdt):
     check(oracle, y, rp, col, val, x, vdt, alpha, beta, y0)
 
 
-@pytest.mark.parametrize("name", ["powerlaw", "mixed_long", "row0_long"])
+@pytest.mark.parametrize("name", ["powerlaw", "mixed_long", "row0_long", "long_rows"])
 @pytest.mark.parametrize("slice_nnz", [0, 5, 300])
 def test_integer_values_bit_exact(pf, oracle, torch_cuda, handle, name, slice_nnz):
     rp, col, _, n = case(name, seed=7)
