@@ -287,7 +287,7 @@ template <typename VT, typename IT, int V>
 static pf_status launch_rowvec(pf_handle h, const SpmvParams<VT, IT> &prm, cudaStream_t st) {
   // U = 2 rows per lane group in flight, built for 4 CTAs per SM (64
   // registers): the best of a sweep over V, U and the CTA bound on configs
-  // 1, 2, 4 and 5
+  // 1, 2 and 5 (rows of 128 or more non-zeros take launch_rowvec_long)
   constexpr int U = 2, NTB = 256, MINB = 4;
   const int64_t rows_per_block = (int64_t)(NTB / 32) * (32 / V) * U;
   const int64_t want = ceil_div(prm.m, rows_per_block);
