@@ -97,8 +97,8 @@ spmm_rowvec_kernel(const SpmmParams<VT, IT> P) {
     const int64_t q0 = s & ~(int64_t)3;
     const int lo = (int)(s - q0);
     const int64_t l64 = e - q0;
-    int len = (int)min(l64, (int64_t)INT32_MAX - 8);
-    if (l64 > (int64_t)INT32_MAX - 8) {
+    int len = (int)min(l64, PF_MAX_ROW_SPAN);
+    if (l64 > PF_MAX_ROW_SPAN) {
       if (lig == 0) atomicOr(P.err, PF_DEVERR_ROWPTR);
       len = 0;
     }

@@ -150,6 +150,12 @@ __device__ void contribute_cut_row(const SpmvParams<VT, IT> &P, int64_t base,
   }
 }
 
+// Longest row (from its first 16-byte block) that the row-vector kernels
+// walk with 32-bit offsets: a lane's offset runs up to two steps of 4 * V
+// (at most 128 each) past the row's end, which must stay below 2^31. Longer
+// rows are flagged PF_DEVERR_ROWPTR and not summed.
+constexpr int64_t PF_MAX_ROW_SPAN = (int64_t)INT32_MAX - 512;
+
 // y = beta*y (all rows empty, Z == 0).
 template <typename VT>
 __global__ void scale_rows_kernel(int64_t m, double beta, VT *__restrict__ y) {

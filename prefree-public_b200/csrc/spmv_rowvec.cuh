@@ -205,7 +205,7 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const DistOut D = DistOut{}) {
       ne[u] = r < P.m ? __ldg(P.row_ptr + r + 1) : IT(0);
     }
     // each row from the 16-byte block q0 holding its first non-zero, with
-    // 32-bit offsets from it (rows longer than 2^31 - 8 non-zeros are flagged,
+    // 32-bit offsets from it (rows longer than PF_MAX_ROW_SPAN are flagged,
     // not summed)
     double acc[U];
     int64_t q0[U];
@@ -219,7 +219,7 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const DistOut D = DistOut{}) {
       q0[u] = (int64_t)s[u] & ~(int64_t)3;
       lo[u] = (int)((int64_t)s[u] - q0[u]);
       const int64_t l64 = (int64_t)e[u] - q0[u];
-      if (l64 > (int64_t)INT32_MAX - 8) {
+      if (l64 > PF_MAX_ROW_SPAN) {
         if (lig == 0) atomicOr(P.err, PF_DEVERR_ROWPTR);
         skip[u] = true;
         len[u] = 0;
