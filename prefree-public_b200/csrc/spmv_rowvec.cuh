@@ -279,7 +279,7 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const DistOut D = DistOut{}) {
       while (more) {
         int4 c4[U];
         VT v4[U][4];
-  #pragma unroll
+#pragma unroll
         for (int u = 0; u < U; ++u) {
           const bool act = o[u] < len[u];
           const int64_t q = q0[u] + o[u];
@@ -287,10 +287,10 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const DistOut D = DistOut{}) {
           Block4<VT>::load(P.val, q, act && o[u] + 1 >= lo[u], act && o[u] + 2 < len[u], v4[u]);
         }
         VT xv[U][4];
-  #pragma unroll
+#pragma unroll
         for (int u = 0; u < U; ++u) {
           const int cc[4] = {c4[u].x, c4[u].y, c4[u].z, c4[u].w};
-  #pragma unroll
+#pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int el = o[u] + i;
             const bool use = el >= lo[u] && el < len[u];
@@ -300,9 +300,9 @@ spmv_rowvec_kernel(const SpmvParams<VT, IT> P, const DistOut D = DistOut{}) {
           }
         }
         more = false;
-  #pragma unroll
+#pragma unroll
         for (int u = 0; u < U; ++u) {
-  #pragma unroll
+#pragma unroll
           for (int i = 0; i < 4; ++i) acc[u] += (double)v4[u][i] * (double)xv[u][i];
           o[u] += 4 * V;
           more |= o[u] < len[u];
